@@ -1,0 +1,581 @@
+"""Layer-operator benchmark: tokens/s and HBM GB/s of one fused layer-op step.
+
+A step is one pass of the hot path over one batch of token rows, on inputs
+already resident in HBM: token-embedding gather (dequantising the table's
+blocks) -> residual-add + RMSNorm -> q/k bias + RoPE -> SwiGLU (-> causal
+softmax rows where the workload defines them).  The default workload is the
+LLaMA-3-8B-shaped prefill (T = 16384 token rows per GPU, hidden 4096, FFN
+14336, 32/8 heads x 128, Q8_0 table [128256, 4096]).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+    python bench.py --impl reference ...   # the reference's CPU operators
+
+For N > 1 launch one process per GPU with torch.distributed.run; every rank
+owns its own contiguous block of token rows (weak scaling: T rows per GPU)
+and the data path has no collective.  Timing: W untimed steps, then K steps
+between a barrier + synchronize on both sides, CUDA events on the launching
+stream, max over ranks.  Inputs are far larger than the 126 MB L2, so no
+flush is needed between steps.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mini-lla_b200")
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+import workloads as wl  # noqa: E402
+
+METRIC = "fused layer-op tokens/s and HBM GB/s vs ~8 TB/s peak at 1/2/4/8 B200"
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(kernel: str, workload: str):
+    """dram bytes per launch of `kernel` recorded from an ncu capture in
+    profiles/<kernel>_<workload>.md (line `traffic_bytes_per_launch: N`)."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Polls SM clock and clock-event reasons through NVML (read-only)
+    while the timed region runs."""
+
+    def __init__(self, device_index: int, interval: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = self._handle(pynvml, device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(
+                self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+        self.interval = interval
+
+    @staticmethod
+    def _handle(nv, cuda_index):
+        """NVML handle of the CUDA device (matched by PCI bus id, since
+        CUDA_VISIBLE_DEVICES renumbers devices)."""
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = "%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id,
+                                        p.pci_device_id)
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(cuda_index)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons |= int(fn(self._h)) & ~0x1
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0}
+        reasons = [n for b, n in REASON_BITS.items() if self.reasons & b]
+        return {"sm_mhz": statistics.median(self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- GPU arm
+
+class LayerStep:
+    """Device buffers and launches of one layer-op step for `tokens` rows."""
+
+    def __init__(self, cfg, device, tokens: int, pos_offset: int):
+        import torch
+        import mlb
+        self.mlb = mlb
+        self.cfg = cfg
+        self.T = tokens
+        self.dev = device
+        self.d = wl.make_inputs(cfg, device, tokens=tokens, pos_offset=pos_offset)
+        max_pos = (pos_offset + tokens - 1) if cfg.positions == "arange" \
+            else cfg.max_position()
+        self.rope_table = torch.from_numpy(
+            mlb.rope_table(cfg.theta, cfg.head_dim, max_pos + 1)).to(device)
+        self.ops = ["embedding", "rmsnorm", "rope", "swiglu"]
+        if cfg.softmax_cols:
+            self.ops.append("softmax")
+
+    def bytes(self):
+        c, t = self.cfg, self.T
+        b = {"embedding": c.bytes_embedding(t), "rmsnorm": c.bytes_rmsnorm(t),
+             "rope": c.bytes_rope(t), "swiglu": c.bytes_swiglu(t)}
+        if c.softmax_cols:
+            b["softmax"] = c.bytes_softmax(t)
+        return b
+
+    def launch(self, op, stream=None, rows=None):
+        """Launches one operator over rows [r0, r1) (all rows by default)."""
+        c, d, m = self.cfg, self.d, self.mlb
+        r0, r1 = (0, self.T) if rows is None else rows
+        if r1 <= r0:
+            return
+        sl = slice(r0, r1)
+        if op == "embedding":
+            m.embedding_rows(d["table"], c.qtype, c.vocab, c.hidden,
+                             d["tokens"][sl], out=d["emb_out"][sl],
+                             status=d["status"], stream=stream)
+        elif op == "rmsnorm":
+            m.rms_norm(d["x"][sl], d["w"], c.eps,
+                       residual=None if d["residual"] is None else d["residual"][sl],
+                       h_out=None if d["h"] is None else d["h"][sl],
+                       out=d["y"][sl], stream=stream)
+        elif op == "rope":
+            m.rope(d["q"][sl], d["k"][sl], d["positions"][sl], self.rope_table,
+                   c.neox, d["bq"], d["bk"], status=d["status"], stream=stream)
+        elif op == "swiglu":
+            m.swiglu(d["gate"][sl], d["up"][sl], out=d["ffn_out"][sl],
+                     stream=stream)
+        elif op == "softmax":
+            h = c.n_heads
+            # rows of head-major scores belonging to tokens [r0, r1)
+            for head in range(h):
+                a, b = head * self.T + r0, head * self.T + r1
+                m.softmax_rows(d["scores"][a:b], d["valid_len"][a:b],
+                               out=d["probs"][a:b], status=d["status"],
+                               stream=stream)
+
+    def step(self, events=None):
+        import torch
+        for i, op in enumerate(self.ops):
+            if events is not None:
+                events[i].record()
+            self.launch(op)
+        if events is not None:
+            events[len(self.ops)].record()
+
+
+def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
+    """The same step end to end through the public API with host buffers:
+    every step copies its inputs from pinned host memory, runs the
+    operators, and reads every result back, pipelined over token chunks on
+    three streams (copy-in, compute, copy-out)."""
+    import torch
+    d, cfg, T = step.d, step.cfg, step.T
+    in_keys = ["tokens", "x", "residual", "q", "k", "positions", "gate", "up"]
+    out_keys = ["emb_out", "h", "y", "q", "k", "ffn_out"]
+    if cfg.softmax_cols:
+        in_keys += ["scores", "valid_len"]
+        out_keys += ["probs"]
+    in_keys = [k for k in in_keys if d.get(k) is not None]
+    out_keys = [k for k in out_keys if d.get(k) is not None]
+    host_in = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
+               for k in in_keys}
+    host_out = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
+                for k in out_keys}
+    for k in in_keys:
+        host_in[k].copy_(d[k])
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    s_in, s_cmp, s_out = (torch.cuda.Stream() for _ in range(3))
+    bounds = [wl.shard_range(T, chunks, c) for c in range(chunks)]
+
+    def rows_of(key, r0, r1):
+        if key in ("scores", "valid_len", "probs"):
+            return None  # head-major rows: copied whole with the last chunk
+        return slice(r0, r1)
+
+    def one_step():
+        done_in = []
+        for c, (r0, r1) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                for k in in_keys:
+                    sl = rows_of(k, r0, r1)
+                    if sl is None:
+                        if c == 0:
+                            d[k].copy_(host_in[k], non_blocking=True)
+                        continue
+                    d[k][sl].copy_(host_in[k][sl], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+                done_in.append(ev)
+        done_cmp = []
+        for c, (r0, r1) in enumerate(bounds):
+            s_cmp.wait_event(done_in[c])
+            for op in step.ops:
+                step.launch(op, stream=s_cmp, rows=(r0, r1))
+            ev = torch.cuda.Event()
+            ev.record(s_cmp)
+            done_cmp.append(ev)
+        for c, (r0, r1) in enumerate(bounds):
+            s_out.wait_event(done_cmp[c])
+            with torch.cuda.stream(s_out):
+                for k in out_keys:
+                    sl = rows_of(k, r0, r1)
+                    if sl is None:
+                        if c == chunks - 1:
+                            host_out[k].copy_(d[k], non_blocking=True)
+                        continue
+                    host_out[k][sl].copy_(d[k][sl], non_blocking=True)
+        s_in.wait_stream(s_out)  # next step's inputs overwrite after readback
+        s_cmp.wait_stream(s_out)
+
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for _ in range(steps):
+        one_step()
+    s_out.wait_stream(s_in)
+    end.record(s_out)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU legs
+
+class CpuLayerSample:
+    """A bounded sample of the workload's token rows on the host, run through
+    the reference's own CPU operators (oracle/_ref, kind "reference") or, if
+    that library is absent, through the C restatement over a thread pool
+    (kind "port")."""
+
+    def __init__(self, cfg, rows: int, seed: int = 0):
+        import numpy as np
+        sys.path.insert(0, ORACLE_DIR)
+        from oracle import REF_SO, Oracle, Reference
+        self.np = np
+        self.cfg = cfg
+        self.rows = rows
+        rng = np.random.default_rng(seed)
+        H, F, hd = cfg.hidden, cfg.ffn, cfg.head_dim
+        self.table = wl.numpy_quant_table(cfg.qtype, cfg.vocab, H, seed)
+        self.tokens = rng.integers(0, cfg.vocab, rows).astype(np.int32)
+        self.x = rng.standard_normal((rows, H), dtype=np.float32)
+        self.r = rng.standard_normal((rows, H), dtype=np.float32)
+        self.w = (rng.standard_normal(H, dtype=np.float32) * 0.1 + 1).astype(np.float32)
+        self.q = rng.standard_normal((rows, cfg.n_heads, hd), dtype=np.float32)
+        self.k = rng.standard_normal((rows, cfg.n_kv_heads, hd), dtype=np.float32)
+        self.pos = np.linspace(0, cfg.max_position(), rows).astype(np.int32)
+        self.g = rng.standard_normal((rows, F), dtype=np.float32)
+        self.u = rng.standard_normal((rows, F), dtype=np.float32)
+        self.bq = (rng.standard_normal(cfg.n_heads * hd, dtype=np.float32) * 0.02
+                   if cfg.bias else None)
+        self.bk = (rng.standard_normal(cfg.n_kv_heads * hd, dtype=np.float32) * 0.02
+                   if cfg.bias else None)
+        self.emb_out = np.empty((rows, H), np.float32)
+        if os.path.exists(REF_SO):
+            self.kind = "reference"
+            self.ref = Reference()
+            lib = self.ref.lib
+            lib.mlref_set_thread_count(0)
+            self.cores = lib.mlref_thread_count()
+            P = lambda a: None if a is None else a.ctypes.data_as(__import__("ctypes").c_void_p)
+            self._P = P
+            self.h_table = lib.mlref_table_new(P(self.table), cfg.qtype, cfg.vocab, H)
+            self.h_x = lib.mlref_rows_new(P(self.x), rows, H)
+            self.h_r = lib.mlref_rows_new(P(self.r), rows, H)
+            self.h_w = lib.mlref_rows_new(P(self.w), 1, H)
+            self.h_q = lib.mlref_heads_new(P(self.q), rows, cfg.n_heads, hd)
+            self.h_k = lib.mlref_heads_new(P(self.k), rows, cfg.n_kv_heads, hd)
+            self.h_g = lib.mlref_rows_new(P(self.g), rows, F)
+            self.h_u = lib.mlref_rows_new(P(self.u), rows, F)
+        else:
+            from concurrent.futures import ThreadPoolExecutor
+            self.kind = "port"
+            self.orc = Oracle()
+            self.cores = os.cpu_count() or 1
+            self.pool = ThreadPoolExecutor(self.cores)
+
+    def step(self):
+        cfg = self.cfg
+        if self.kind == "reference":
+            lib, P = self.ref.lib, self._P
+            lib.mlref_bench_embedding(self.h_table, P(self.tokens), self.rows,
+                                      P(self.emb_out))
+            lib.mlref_bench_rmsnorm(self.h_x, self.h_r if cfg.residual else None,
+                                    self.h_w, cfg.eps)
+            lib.mlref_bench_rope(self.h_q, self.h_k, P(self.bq), P(self.bk),
+                                 P(self.pos), cfg.theta, int(cfg.neox))
+            lib.mlref_bench_swiglu(self.h_g, self.h_u)
+            return
+        n = self.cores
+        parts = [wl.shard_range(self.rows, n, i) for i in range(n)]
+        orc = self.orc
+
+        def work(a, b):
+            if b <= a:
+                return
+            orc.embedding(self.table, cfg.qtype, cfg.vocab, cfg.hidden,
+                          self.tokens[a:b])
+            orc.rmsnorm(self.x[a:b], self.w, cfg.eps,
+                        residual=self.r[a:b] if cfg.residual else None)
+            orc.rope(self.q[a:b], self.k[a:b], self.pos[a:b], cfg.theta,
+                     int(cfg.neox), self.bq, self.bk)
+            orc.swiglu(self.g[a:b], self.u[a:b])
+        list(self.pool.map(lambda ab: work(*ab), parts))
+
+
+def cpu_sample_rows(cfg, budget_s: float, steps: int):
+    """Rows per step so that `steps` CPU steps take about `budget_s`."""
+    probe = CpuLayerSample(cfg, 256)
+    probe.step()
+    t0 = time.perf_counter()
+    probe.step()
+    per_row = (time.perf_counter() - t0) / 256
+    rows = int(budget_s / max(steps, 1) / max(per_row, 1e-9))
+    return max(64, min(cfg.tokens, rows)), probe.kind
+
+
+def run_cpu(cfg, steps: int, warmup: int, budget_s: float):
+    rows, _ = cpu_sample_rows(cfg, budget_s, steps)
+    sample = CpuLayerSample(cfg, rows)
+    for _ in range(warmup):
+        sample.step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        sample.step()
+    sec = (time.perf_counter() - t0) / steps
+    ops_bytes = (cfg.bytes_embedding(rows) + cfg.bytes_rmsnorm(rows) +
+                 cfg.bytes_rope(rows) + cfg.bytes_swiglu(rows))
+    return {"tokens_per_s": rows / sec, "gbs": ops_bytes / sec / 1e9,
+            "rows": rows, "sec_per_step": sec, "kind": sample.kind,
+            "cores": sample.cores}
+
+
+def reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    warm = max(1, min(args.warmup, 3))
+    res = run_cpu(cfg, args.steps, warm, budget_s=args.cpu_budget)
+    sample = (f"{res['rows']} of {cfg.tokens} token rows of {cfg.name} per step "
+              f"(embedding, {'residual ' if cfg.residual else ''}RMSNorm, RoPE, "
+              f"SwiGLU), reference ops called per row inside its ParallelFor")
+    line = {
+        "metric": METRIC, "impl": "reference",
+        "value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": warm,
+        "ms_per_step": round(res["sec_per_step"] * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": config_block(cfg, args, cfg.tokens),
+        "hbm_gbs_equiv": round(res["gbs"], 2),
+        "cpu_baseline": {"value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
+                         "cores": res["cores"], "kind": res["kind"],
+                         "sample": sample},
+        "e2e": {"value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(cfg, args, tokens_per_gpu):
+    return {
+        "workload": cfg.name, "tokens_per_gpu": tokens_per_gpu,
+        "global_tokens": tokens_per_gpu * args.gpus, "hidden": cfg.hidden,
+        "ffn": cfg.ffn, "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads,
+        "head_dim": cfg.head_dim, "rope": "neox" if cfg.neox else "normal",
+        "rope_theta": cfg.theta, "qk_bias": cfg.bias,
+        "residual_rmsnorm": cfg.residual, "eps": cfg.eps,
+        "embedding": f"{wl.QNAME[cfg.qtype]} [{cfg.vocab}, {cfg.hidden}]",
+        "parallelism": f"token-range shards x{args.gpus}, replicated weights, "
+                       "no collective",
+        "l2": "inputs larger than L2 (126 MB); no flush",
+    }
+
+
+# ---------------------------------------------------------------- main
+
+def gpu_arm(args, cfg):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    # weak scaling: every GPU owns a block of cfg.tokens rows (positions of a
+    # sequence each); --strong splits one batch of cfg.tokens rows instead.
+    if args.strong:
+        r0, r1 = wl.shard_range(cfg.tokens, world, rank)
+        tokens, pos_offset = r1 - r0, r0
+    else:
+        tokens, pos_offset = cfg.tokens, 0
+    step = LayerStep(cfg, dev, tokens, pos_offset)
+    nops = len(step.ops)
+    op_bytes = step.bytes()
+    for _ in range(args.warmup):
+        step.step()
+    torch.cuda.synchronize()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
+              for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        for i in range(args.steps):
+            step.step(events[i])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    total_ms = events[0][0].elapsed_time(events[-1][nops])
+    op_ms = [sum(events[i][j].elapsed_time(events[i][j + 1])
+                 for i in range(args.steps)) / args.steps for j in range(nops)]
+    bits = torch.zeros(1, dtype=torch.int32)
+    bits.copy_(step.d["status"])
+    if int(bits.item()) != 0:
+        raise RuntimeError(f"device status raised: {int(bits.item())}")
+    e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps)
+    stats = torch.tensor([total_ms, e2e_ms] + op_ms, dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    stats = stats.cpu().tolist()
+    total_ms, e2e_ms, op_ms = stats[0], stats[1], stats[2:]
+    clocks = sampler.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu(cfg, 3, 1, budget_s=args.cpu_budget / 2)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    ms_step = total_ms / args.steps
+    tokens_all = tokens * world
+    value = tokens_all / (ms_step / 1e3)
+    step_bytes = sum(op_bytes.values())
+    peak, peak_kind = measured_peak()
+    gbs_per_gpu = step_bytes / (ms_step / 1e3) / 1e9
+    ops = {}
+    for j, op in enumerate(step.ops):
+        g = op_bytes[op] / (op_ms[j] / 1e3) / 1e9
+        ops[op] = {"ms": round(op_ms[j], 4), "gbs": round(g, 1),
+                   "frac_of_measured": round(g / peak, 4),
+                   "frac_of_8tbs": round(g / SPEC_HBM_GBS, 4),
+                   "bytes": op_bytes[op]}
+    dom = max(step.ops, key=lambda o: op_bytes[o])
+    j = step.ops.index(dom)
+    achieved = op_bytes[dom] / (op_ms[j] / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": config_block(cfg, args, tokens),
+        "hbm_gbs": round(gbs_per_gpu * world, 1),
+        "hbm_gbs_per_gpu": round(gbs_per_gpu, 1),
+        "hbm_frac_of_measured": round(gbs_per_gpu / peak, 4),
+        "hbm_frac_of_8tbs": round(gbs_per_gpu / SPEC_HBM_GBS, 4),
+        "ops": ops,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4),
+                     "traffic": profile_traffic(dom, cfg.name),
+                     "algorithmic_bytes": op_bytes[dom]},
+        "clocks": clocks,
+        "e2e": {"value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": args.steps * sum(
+            step.cfg.n_heads if o == "softmax" else 1 for o in step.ops),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {
+            "value": round(cpu["tokens_per_s"], 1), "unit": "tokens/s",
+            "cores": cpu["cores"], "kind": cpu["kind"],
+            "sample": f"{cpu['rows']} of {cfg.tokens} token rows per step, 3 steps"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="llama3-8b-t16384",
+                    choices=sorted(wl.CONFIGS))
+    ap.add_argument("--impl", default="mlb", choices=["mlb", "reference"])
+    ap.add_argument("--strong", action="store_true",
+                    help="split one batch of T rows across GPUs")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=20.0,
+                    help="seconds of CPU work for the CPU legs")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = wl.CONFIGS[args.workload]
+    if args.impl == "reference":
+        reference_arm(args, cfg)
+    else:
+        gpu_arm(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

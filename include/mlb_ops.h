@@ -1,0 +1,183 @@
+/*
+ * mlb_ops.h — C ABI of the B200 (sm_100a) layer-operator library libmlb.so.
+ *
+ * These entry points are what mini-lla's GPU operator layer binds to in place
+ * of its per-vector kernels (reference src/cuda_ops.cu and the declarations
+ * in include/mini_llama/cuda_ops.h:11-34).  The C++17 wrappers that keep the
+ * reference's CudaRmsNorm / CudaRope / ... signatures call them with rows = 1;
+ * row-batched callers (prefill) call them with rows = T.
+ *
+ * Conventions (all entries):
+ *   - Every pointer argument is a DEVICE pointer unless the name ends in
+ *     _host; the caller owns every buffer.  Nothing here allocates device
+ *     memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Calls are asynchronous on that stream and run on the device
+ *     that is current on the calling thread; the stream must belong to it.
+ *   - Return value: MLB_OK, or MLB_ERR_ARG for a rejected argument (nothing is
+ *     launched), or MLB_ERR_CUDA when the launch failed.  The message of the
+ *     last failure on the calling thread is mlb_last_error().
+ *   - Conditions only the device can see (a token id outside the table, a
+ *     position outside the RoPE table, a softmax row length outside [1, cols])
+ *     are reported through an optional device status word: the kernel ORs the
+ *     MLB_STATUS_* bits into *status (the caller zeroes it and reads it after
+ *     the stream synchronises).  The affected rows are skipped (RoPE) or
+ *     written as zeros (embedding, softmax); other rows are unaffected.
+ *   - Element counts are int64_t; fp32 tensors are row-major and contiguous.
+ *   - Floating-point results follow the reference CPU arithmetic of
+ *     src/ops.cc and src/quant.cc: bit-exact for the embedding gather, the
+ *     residual sum and RoPE; within 1e-5 relative error for RMSNorm's output,
+ *     SiLU/SwiGLU and softmax (whose sums are reduced in a different order and
+ *     whose exponential is CUDA's expf).
+ *   - No entry point falls back to the CPU.
+ */
+#ifndef MLB_OPS_H_
+#define MLB_OPS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MLB_OK = 0,
+  MLB_ERR_ARG = 1,
+  MLB_ERR_CUDA = 2,
+  MLB_ERR_RANGE = 3 /* returned by host-side helpers that read the status */
+};
+
+/* Status bits written by kernels into the optional device status word. */
+enum {
+  MLB_STATUS_BAD_TOKEN = 1,    /* embedding: token id < 0 or >= vocab      */
+  MLB_STATUS_BAD_POSITION = 2, /* rope: position < 0 or >= table rows     */
+  MLB_STATUS_BAD_LENGTH = 4    /* softmax: valid length outside [1, cols] */
+};
+
+/* Table formats; same order as the reference's QuantType
+ * (include/mini_llama/quantized_tensor.h:13) and its ggml block layouts
+ * (quantized_tensor.h:19-35): Q8_0 34 B, Q4_0 18 B, Q4_1 20 B per 32 values. */
+enum { MLB_F32 = 0, MLB_Q8_0 = 1, MLB_Q4_0 = 2, MLB_Q4_1 = 3 };
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int mlb_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* mlb_last_error(void);
+
+/* Bytes of one table row: ceil(cols / 32) blocks, or cols floats for F32. */
+int64_t mlb_row_bytes(int qtype, int64_t cols);
+
+/*
+ * (Residual-add +) RMSNorm over rows.
+ * Replaces CudaRmsNorm (cuda_ops.h:12-13, cuda_ops.cu:193-204) and, fused,
+ * the CudaAdd that precedes it in the layer (cuda_forward.cc:72-77, 83;
+ * CPU composition forward.cc:122-124 -> ops.cc:117-124, 68-81):
+ *   h[r] = x[r] + residual[r]            (bit-exact; skipped if residual NULL)
+ *   y[r] = h[r] * (1 / sqrt(sum(h[r]^2) / cols + eps)) * w
+ * residual and h_out may be NULL; with residual NULL the norm is of x.
+ * x, residual, h_out and y are [rows, cols]; w is [cols].  h_out may alias x
+ * or residual; y may alias x.  One pass over memory.
+ */
+int mlb_rmsnorm_f32(const float* x, const float* residual, float* h_out,
+                    float* y, const float* w, int64_t rows, int64_t cols,
+                    float eps, void* stream);
+
+/*
+ * SwiGLU over n = rows * cols elements: out = (g / (1 + exp(-g))) * u.
+ * Replaces CudaSilu + CudaMul (cuda_ops.h:19-22, cuda_ops.cu:222-240, used
+ * together at cuda_forward.cc:80-82; CPU ops.cc:100-115).  One pass.
+ * out may alias gate or up.
+ */
+int mlb_swiglu_f32(const float* gate, const float* up, float* out,
+                   int64_t rows, int64_t cols, void* stream);
+
+/* SiLU alone, out = x / (1 + exp(-x)); replaces CudaSilu (cuda_ops.h:19). */
+int mlb_silu_f32(const float* x, float* out, int64_t n, void* stream);
+
+/* Element-wise product; replaces CudaMul (cuda_ops.h:22). */
+int mlb_mul_f32(const float* a, const float* b, float* out, int64_t n,
+                void* stream);
+
+/* Element-wise sum; replaces CudaAdd (cuda_ops.h:25). Bit-exact. */
+int mlb_add_f32(const float* a, const float* b, float* out, int64_t n,
+                void* stream);
+
+/*
+ * Bias add over rows: out[r] = value[r] + bias (a copy when bias is NULL).
+ * Replaces CudaAddBias (cuda_ops.h:34, cuda_ops.cu:298-308). Bit-exact.
+ */
+int mlb_add_bias_f32(const float* value, const float* bias, float* out,
+                     int64_t rows, int64_t cols, void* stream);
+
+/*
+ * Host-side (cos, sin) table for RoPE, bit-identical to the values the
+ * reference computes inline (ops.cc:26-31 normal, :45-50 NeoX; the two
+ * exponent expressions give the same float):
+ *   angle(p, j) = (float)p / powf(theta, (float)(2j) / (float)hd)
+ *   out_host[((p - pos_begin) * hd/2 + j) * 2 + {0,1}] = {cosf, sinf}(angle)
+ * for p in [pos_begin, pos_end), j in [0, hd/2).  Computed with the host's
+ * libm so it matches the reference CPU path on the same machine.
+ */
+int mlb_rope_table_build_host(float theta, int hd, int64_t pos_begin,
+                              int64_t pos_end, float* out_host);
+
+/*
+ * Attention-bias add + rotary embedding, in place, for a batch of tokens.
+ * Replaces CudaAddBias(q/k) + CudaRope (cuda_ops.h:15-17, 34;
+ * cuda_ops.cu:206-220, 298-308; CPU forward.cc:113-119 -> ops.cc:126-142).
+ *   q: [rows, nq, hd], k: [rows, nk, hd]  (k may be NULL when nk == 0)
+ *   bq: [nq*hd] or NULL, bk: [nk*hd] or NULL (added before rotation)
+ *   positions: [rows] int32; cos_sin: table from mlb_rope_table_build_host
+ *   with table_rows positions starting at position 0.
+ *   neox = 0: pairs (2j, 2j+1); neox = 1: pairs (j, j + hd/2).
+ * x0' = x0*c - x1*s, x1' = x0*s + x1*c with separate roundings: bit-exact.
+ * A token whose position is outside [0, table_rows) gets its bias added but
+ * is not rotated, and MLB_STATUS_BAD_POSITION is raised.
+ */
+int mlb_rope_f32(float* q, float* k, const float* bq, const float* bk,
+                 const int32_t* positions, const float* cos_sin,
+                 int64_t table_rows, int64_t rows, int nq, int nk, int hd,
+                 int neox, int32_t* status, void* stream);
+
+/*
+ * Row softmax over the first valid_len[r] entries of each row, zeros after
+ * (valid_len NULL = full rows).  Replaces CudaSoftmax (cuda_ops.h:28,
+ * cuda_ops.cu:253-262; CPU ops.cc:83-98) and the per-head softmax of the
+ * causal attention rows (forward.cc:53-63).  x, y: [rows, cols]; y may
+ * alias x.  A row whose length is outside [1, cols] is written as zeros and
+ * raises MLB_STATUS_BAD_LENGTH.
+ */
+int mlb_softmax_rows_f32(const float* x, float* y, int64_t rows, int64_t cols,
+                         const int32_t* valid_len, int32_t* status,
+                         void* stream);
+
+/*
+ * Token-embedding gather with in-register block dequantisation.
+ * Replaces CudaEmbeddingRow (cuda_ops.h:31, cuda_ops.cu:146-189, 264-296;
+ * CPU forward.cc:29-33 -> quant.cc:278-304).
+ *   table: vocab rows of mlb_row_bytes(qtype, cols) bytes, ggml blocks as
+ *   the reference stores them (a partial tail block when cols % 32 != 0).
+ *   tokens: [rows] int32; out: [rows, cols] fp32.
+ *   Q8_0: d*q;  Q4_0: d*(nib-8);  Q4_1: d*nib + m  (fp16 d, m decoded as in
+ *   quant.cc:44-71).  Bit-exact with the reference.
+ * A token outside [0, vocab) writes a zero row and raises
+ * MLB_STATUS_BAD_TOKEN.
+ */
+int mlb_embedding_gather(const void* table, int qtype, int64_t vocab,
+                         int64_t cols, const int32_t* tokens, int64_t rows,
+                         float* out, int32_t* status, void* stream);
+
+/*
+ * Helper for synchronous callers: waits for `stream`, copies the device
+ * status word to the host, and returns MLB_OK when it is zero, MLB_ERR_RANGE
+ * when a bit is set (the bits are stored in *bits_host when non-NULL), or
+ * MLB_ERR_CUDA.  Does not clear the word.
+ */
+int mlb_status_check(const int32_t* status, int32_t* bits_host, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLB_OPS_H_ */

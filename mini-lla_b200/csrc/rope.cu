@@ -1,0 +1,188 @@
+// Attention-bias add + rotary position embedding, in place, for a batch of
+// tokens, Q and K in one launch.
+//
+// Reference arithmetic (src/forward.cc:113-119 AddBias then src/ops.cc:126-142
+// Rope -> ApplyRopeNormal :22-37 / ApplyRopeNeoX :40-56):
+//   q += bq; k += bk                      (skipped when the bias is absent)
+//   x0' = x0*cos - x1*sin;  x1' = x0*sin + x1*cos
+// pairs (2j, 2j+1) in the normal layout, (j, j + hd/2) in NeoX.  cos/sin come
+// from a table built on the host with the reference's own expressions
+// (rope_table.cc), so device code never evaluates powf/cosf/sinf and the
+// result is bit-exact: the multiplies and the add/subtract are separate
+// IEEE roundings (__fmul_rn / __fadd_rn / __fsub_rn, no contraction).
+//
+// Layout: q [rows, nq, hd], k [rows, nk, hd] fp32; positions [rows] int32;
+// table [table_rows, hd/2] of (cos, sin) float pairs (8 MB at 16384
+// positions x hd 128, which stays resident in the 126 MB L2).
+// Work item = one token x one head x one group of 4 rotated floats pairs:
+//   normal: a float4 holds pairs 2g, 2g+1 -> table float4 (c,s,c,s)
+//   NeoX:   float4s at g*4 and hd/2 + g*4 hold pairs 4g..4g+3 -> two table
+//           float4s
+// One CTA walks the (head, group) items of a token, grid-strides tokens.
+// HBM roofline: 8 bytes per rotated float plus the position (and the bias
+// vectors once, L2-resident afterwards).
+#include <climits>
+
+#include "common.cuh"
+
+namespace mlb {
+namespace {
+
+struct RopeArgs {
+  float* q;
+  float* k;
+  const float* bq;
+  const float* bk;
+  const int32_t* positions;
+  const float* table;
+  int64_t table_rows;
+  int64_t rows;
+  int nq;
+  int nk;
+  int hd;
+  int32_t* status;
+};
+
+__device__ __forceinline__ void Rotate(float& x0, float& x1, float c, float s) {
+  const float first = x0;
+  const float second = x1;
+  x0 = __fsub_rn(__fmul_rn(first, c), __fmul_rn(second, s));
+  x1 = __fadd_rn(__fmul_rn(first, s), __fmul_rn(second, c));
+}
+
+// Vector path: hd % 8 == 0 (NeoX) or hd % 4 == 0 (normal), 16-byte aligned.
+template <bool NEOX>
+__global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
+  const int half = a.hd >> 1;
+  const int groups = NEOX ? (a.hd >> 3) : (a.hd >> 2);  // per head
+  const int heads = a.nq + a.nk;
+  const int items = heads * groups;
+  for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
+    const int32_t pos = __ldg(a.positions + t);
+    const bool ok = pos >= 0 && pos < a.table_rows;
+    if (!ok && threadIdx.x == 0 && a.status != nullptr)
+      atomicOr(a.status, MLB_STATUS_BAD_POSITION);
+    const float4* trow = reinterpret_cast<const float4*>(
+        a.table + static_cast<size_t>(ok ? pos : 0) * a.hd);
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+      const int head = it / groups;
+      const int g = it - head * groups;
+      const bool is_q = head < a.nq;
+      const int h = is_q ? head : head - a.nq;
+      float* base = is_q ? a.q + (static_cast<size_t>(t) * a.nq + h) * a.hd
+                         : a.k + (static_cast<size_t>(t) * a.nk + h) * a.hd;
+      const float* bias = is_q ? a.bq : a.bk;
+      if (NEOX) {
+        float4* lo = reinterpret_cast<float4*>(base + 4 * g);
+        float4* hi = reinterpret_cast<float4*>(base + half + 4 * g);
+        float4 x0 = LoadStream(lo);
+        float4 x1 = LoadStream(hi);
+        if (bias != nullptr) {
+          const float* bh = bias + static_cast<size_t>(h) * a.hd;
+          x0 = AddRn(x0, __ldg(reinterpret_cast<const float4*>(bh + 4 * g)));
+          x1 = AddRn(x1, __ldg(reinterpret_cast<const float4*>(bh + half + 4 * g)));
+        }
+        if (ok) {
+          const float4 cs0 = __ldg(trow + 2 * g);      // pairs 4g, 4g+1
+          const float4 cs1 = __ldg(trow + 2 * g + 1);  // pairs 4g+2, 4g+3
+          Rotate(x0.x, x1.x, cs0.x, cs0.y);
+          Rotate(x0.y, x1.y, cs0.z, cs0.w);
+          Rotate(x0.z, x1.z, cs1.x, cs1.y);
+          Rotate(x0.w, x1.w, cs1.z, cs1.w);
+        }
+        StoreStream(lo, x0);
+        StoreStream(hi, x1);
+      } else {
+        float4* p = reinterpret_cast<float4*>(base + 4 * g);
+        float4 x = LoadStream(p);
+        if (bias != nullptr) {
+          const float* bh = bias + static_cast<size_t>(h) * a.hd;
+          x = AddRn(x, __ldg(reinterpret_cast<const float4*>(bh + 4 * g)));
+        }
+        if (ok) {
+          const float4 cs = __ldg(trow + g);  // pairs 2g, 2g+1
+          Rotate(x.x, x.y, cs.x, cs.y);
+          Rotate(x.z, x.w, cs.z, cs.w);
+        }
+        StoreStream(p, x);
+      }
+    }
+  }
+}
+
+// Any even hd / alignment: one item per rotated pair.
+__global__ void __launch_bounds__(256) RopeScalarKernel(RopeArgs a, int neox) {
+  const int half = a.hd >> 1;
+  const int heads = a.nq + a.nk;
+  const int items = heads * half;
+  for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
+    const int32_t pos = a.positions[t];
+    const bool ok = pos >= 0 && pos < a.table_rows;
+    if (!ok && threadIdx.x == 0 && a.status != nullptr)
+      atomicOr(a.status, MLB_STATUS_BAD_POSITION);
+    const float* trow = a.table + static_cast<size_t>(ok ? pos : 0) * a.hd;
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+      const int head = it / half;
+      const int j = it - head * half;
+      const bool is_q = head < a.nq;
+      const int h = is_q ? head : head - a.nq;
+      float* base = is_q ? a.q + (static_cast<size_t>(t) * a.nq + h) * a.hd
+                         : a.k + (static_cast<size_t>(t) * a.nk + h) * a.hd;
+      const float* bias = is_q ? a.bq : a.bk;
+      const int i0 = neox ? j : 2 * j;
+      const int i1 = neox ? j + half : 2 * j + 1;
+      float x0 = base[i0];
+      float x1 = base[i1];
+      if (bias != nullptr) {
+        const float* bh = bias + static_cast<size_t>(h) * a.hd;
+        x0 = __fadd_rn(x0, bh[i0]);
+        x1 = __fadd_rn(x1, bh[i1]);
+      }
+      if (ok) Rotate(x0, x1, trow[2 * j], trow[2 * j + 1]);
+      base[i0] = x0;
+      base[i1] = x1;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace mlb
+
+extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
+                            const float* bk, const int32_t* positions,
+                            const float* cos_sin, int64_t table_rows,
+                            int64_t rows, int nq, int nk, int hd, int neox,
+                            int32_t* status, void* stream) {
+  using namespace mlb;
+  if (rows < 0 || nq < 0 || nk < 0 || hd <= 0 || (hd % 2) != 0 ||
+      table_rows < 0)
+    return Fail(MLB_ERR_ARG, "mlb_rope_f32: bad shape (hd must be even)");
+  if (static_cast<int64_t>(nq + static_cast<int64_t>(nk)) * hd > INT_MAX)
+    return Fail(MLB_ERR_ARG, "mlb_rope_f32: too many heads");
+  if (rows == 0 || nq + nk == 0) return MLB_OK;
+  if (positions == nullptr || cos_sin == nullptr || (nq > 0 && q == nullptr) ||
+      (nk > 0 && k == nullptr))
+    return Fail(MLB_ERR_ARG, "mlb_rope_f32: null pointer");
+  RopeArgs a{q, k, bq, bk, positions, cos_sin, table_rows, rows, nq, nk, hd,
+             status};
+  const bool aligned = (nq == 0 || Aligned16(q)) && (nk == 0 || Aligned16(k)) &&
+                       (bq == nullptr || Aligned16(bq)) &&
+                       (bk == nullptr || Aligned16(bk)) && Aligned16(cos_sin);
+  const bool vec = aligned && (neox ? (hd % 8) == 0 : (hd % 4) == 0);
+  const int64_t cap = 1 << 24;
+  const dim3 grid(static_cast<unsigned>(rows < cap ? rows : cap));
+  const int items = (nq + nk) * (neox ? hd / 8 : hd / 4);
+  int threads = items < 256 ? (items + 31) / 32 * 32 : 256;
+  if (threads < 32) threads = 32;
+  cudaStream_t s = AsStream(stream);
+  if (vec) {
+    if (neox) {
+      RopeVecKernel<true><<<grid, threads, 0, s>>>(a);
+    } else {
+      RopeVecKernel<false><<<grid, threads, 0, s>>>(a);
+    }
+  } else {
+    RopeScalarKernel<<<grid, 256, 0, s>>>(a, neox);
+  }
+  return CheckLaunch("mlb_rope_f32");
+}

@@ -1,0 +1,289 @@
+"""ctypes binding of libmlb.so (include/mlb_ops.h) for Python callers.
+
+Tensors are torch CUDA tensors (torch supplies device memory and streams);
+every call goes straight to the C ABI and from there to the sm_100a kernels.
+There is no CPU fallback: loading fails loudly when libmlb.so is missing.
+
+Error behaviour follows the reference's C++ operator layer
+(src/cuda_ops.cu): a shape mismatch raises ValueError (std::invalid_argument
+there), an out-of-range token or position reported by the device raises
+IndexError (std::out_of_range), a CUDA failure raises RuntimeError
+(std::runtime_error from CudaCheckLastError).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int, c_int64, c_void_p
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmlb.so")
+
+F32, Q8_0, Q4_0, Q4_1 = 0, 1, 2, 3
+QTYPE_NAMES = {"F32": F32, "Q8_0": Q8_0, "Q4_0": Q4_0, "Q4_1": Q4_1}
+STATUS_BAD_TOKEN, STATUS_BAD_POSITION, STATUS_BAD_LENGTH = 1, 2, 4
+
+# Every symbol include/mlb_ops.h declares, with (restype, argtypes).
+SIGNATURES = {
+    "mlb_version": (c_int, []),
+    "mlb_last_error": (ctypes.c_char_p, []),
+    "mlb_row_bytes": (c_int64, [c_int, c_int64]),
+    "mlb_rmsnorm_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_int64, c_int64, c_float, c_void_p]),
+    "mlb_swiglu_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                               c_void_p]),
+    "mlb_silu_f32": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "mlb_mul_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "mlb_add_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "mlb_add_bias_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64,
+                                 c_int64, c_void_p]),
+    "mlb_rope_table_build_host": (c_int, [c_float, c_int, c_int64, c_int64,
+                                          c_void_p]),
+    "mlb_rope_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_int64, c_int64, c_int, c_int, c_int,
+                             c_int, c_void_p, c_void_p]),
+    "mlb_softmax_rows_f32": (c_int, [c_void_p, c_void_p, c_int64, c_int64,
+                                     c_void_p, c_void_p, c_void_p]),
+    "mlb_embedding_gather": (c_int, [c_void_p, c_int, c_int64, c_int64,
+                                     c_void_p, c_int64, c_void_p, c_void_p,
+                                     c_void_p]),
+    "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads libmlb.so once and binds every declared symbol."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"libmlb.so not found at {path}: build it with "
+            "`make -C mini-lla_b200` (there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def _ptr(t):
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return c_void_p(stream.cuda_stream)
+
+
+def _check(rc: int, op: str):
+    if rc == 0:
+        return
+    msg = load().mlb_last_error().decode()
+    if rc == 1:
+        raise ValueError(f"{op}: {msg}")
+    if rc == 3:
+        raise IndexError(f"{op}: {msg}")
+    raise RuntimeError(f"{op}: {msg}")
+
+
+def _require(cond: bool, op: str, what: str):
+    if not cond:
+        raise ValueError(f"{op}: {what}")
+
+
+def _f32_cuda(t, op, name):
+    import torch
+    _require(t.is_cuda and t.dtype == torch.float32 and t.is_contiguous(), op,
+             f"{name} must be a contiguous float32 CUDA tensor")
+
+
+def row_bytes(qtype: int, cols: int) -> int:
+    return int(load().mlb_row_bytes(qtype, cols))
+
+
+def rms_norm(x, weight, eps: float, residual=None, h_out=None, out=None,
+             stream=None):
+    """y = RmsNorm(x [+ residual]) row-wise over the last dim; returns y.
+
+    With `residual`, the sum h = x + residual is also written to `h_out`
+    when given (the new residual stream)."""
+    op = "rms_norm"
+    _f32_cuda(x, op, "x")
+    _f32_cuda(weight, op, "weight")
+    cols = x.shape[-1]
+    _require(weight.numel() == cols, op, "weight size mismatch")
+    if residual is not None:
+        _f32_cuda(residual, op, "residual")
+        _require(residual.shape == x.shape, op, "residual shape mismatch")
+    if h_out is not None:
+        _f32_cuda(h_out, op, "h_out")
+        _require(h_out.shape == x.shape, op, "h_out shape mismatch")
+    if out is None:
+        import torch
+        out = torch.empty_like(x)
+    rows = x.numel() // cols if cols else 0
+    _check(load().mlb_rmsnorm_f32(_ptr(x), _ptr(residual), _ptr(h_out),
+                                  _ptr(out), _ptr(weight), rows, cols,
+                                  float(eps), _stream(stream)), op)
+    return out
+
+
+def swiglu(gate, up, out=None, stream=None):
+    op = "swiglu"
+    _f32_cuda(gate, op, "gate")
+    _f32_cuda(up, op, "up")
+    _require(gate.shape == up.shape, op, "shape mismatch")
+    if out is None:
+        import torch
+        out = torch.empty_like(gate)
+    cols = gate.shape[-1] if gate.dim() else 1
+    rows = gate.numel() // cols if cols else 0
+    _check(load().mlb_swiglu_f32(_ptr(gate), _ptr(up), _ptr(out), rows, cols,
+                                 _stream(stream)), op)
+    return out
+
+
+def silu(x, out=None, stream=None):
+    _f32_cuda(x, "silu", "x")
+    if out is None:
+        import torch
+        out = torch.empty_like(x)
+    _check(load().mlb_silu_f32(_ptr(x), _ptr(out), x.numel(), _stream(stream)),
+           "silu")
+    return out
+
+
+def mul(a, b, out=None, stream=None):
+    _f32_cuda(a, "mul", "a")
+    _f32_cuda(b, "mul", "b")
+    _require(a.numel() == b.numel(), "mul", "size mismatch")
+    if out is None:
+        import torch
+        out = torch.empty_like(a)
+    _check(load().mlb_mul_f32(_ptr(a), _ptr(b), _ptr(out), a.numel(),
+                              _stream(stream)), "mul")
+    return out
+
+
+def add(a, b, out=None, stream=None):
+    _f32_cuda(a, "add", "a")
+    _f32_cuda(b, "add", "b")
+    _require(a.numel() == b.numel(), "add", "size mismatch")
+    if out is None:
+        import torch
+        out = torch.empty_like(a)
+    _check(load().mlb_add_f32(_ptr(a), _ptr(b), _ptr(out), a.numel(),
+                              _stream(stream)), "add")
+    return out
+
+
+def add_bias(value, bias=None, out=None, stream=None):
+    _f32_cuda(value, "add_bias", "value")
+    cols = value.shape[-1]
+    if bias is not None:
+        _f32_cuda(bias, "add_bias", "bias")
+        _require(bias.numel() == cols, "add_bias", "bias shape mismatch")
+    if out is None:
+        import torch
+        out = torch.empty_like(value)
+    rows = value.numel() // cols if cols else 0
+    _check(load().mlb_add_bias_f32(_ptr(value), _ptr(bias), _ptr(out), rows,
+                                   cols, _stream(stream)), "add_bias")
+    return out
+
+
+def rope_table(theta: float, head_dim: int, positions: int, pos_begin: int = 0):
+    """Host-built (cos, sin) table as a numpy float32 array [P, head_dim]."""
+    import numpy as np
+    table = np.empty((positions, head_dim), dtype=np.float32)
+    rc = load().mlb_rope_table_build_host(
+        float(theta), int(head_dim), int(pos_begin), int(pos_begin + positions),
+        table.ctypes.data_as(c_void_p))
+    if rc != 0:
+        raise ValueError("rope_table: invalid theta, head_dim or range")
+    return table
+
+
+def rope(q, k, positions, table, neox: bool, bq=None, bk=None, status=None,
+         stream=None):
+    """In-place bias add + RoPE on q [T, nq, hd] and k [T, nk, hd]."""
+    import torch
+    op = "rope"
+    _f32_cuda(q, op, "q")
+    _require(q.dim() == 3, op, "q must be [tokens, heads, head_dim]")
+    rows, nq, hd = q.shape
+    nk = 0
+    if k is not None:
+        _f32_cuda(k, op, "k")
+        _require(k.dim() == 3 and k.shape[0] == rows and k.shape[2] == hd, op,
+                 "k must be [tokens, kv_heads, head_dim]")
+        nk = k.shape[1]
+    _require(hd % 2 == 0, op, "expected [heads, even_dim]")
+    _require(positions.is_cuda and positions.dtype == torch.int32 and
+             positions.numel() == rows, op, "positions must be int32 [tokens]")
+    _f32_cuda(table, op, "table")
+    _require(table.dim() == 2 and table.shape[1] == hd, op,
+             "table must be [positions, head_dim]")
+    for b, n, name in ((bq, nq, "bq"), (bk, nk, "bk")):
+        if b is not None:
+            _f32_cuda(b, op, name)
+            _require(b.numel() == n * hd, op, f"{name} shape mismatch")
+    _check(load().mlb_rope_f32(_ptr(q), _ptr(k), _ptr(bq), _ptr(bk),
+                               _ptr(positions), _ptr(table), table.shape[0],
+                               rows, nq, nk, hd, 1 if neox else 0,
+                               _ptr(status), _stream(stream)), op)
+
+
+def softmax_rows(x, valid_len=None, out=None, status=None, stream=None):
+    import torch
+    op = "softmax_rows"
+    _f32_cuda(x, op, "x")
+    cols = x.shape[-1]
+    _require(x.numel() > 0 and cols > 0, op, "expected a non-empty vector")
+    rows = x.numel() // cols
+    if valid_len is not None:
+        _require(valid_len.is_cuda and valid_len.dtype == torch.int32 and
+                 valid_len.numel() == rows, op, "valid_len must be int32 [rows]")
+    if out is None:
+        out = torch.empty_like(x)
+    _check(load().mlb_softmax_rows_f32(_ptr(x), _ptr(out), rows, cols,
+                                       _ptr(valid_len), _ptr(status),
+                                       _stream(stream)), op)
+    return out
+
+
+def embedding_rows(table, qtype: int, vocab: int, cols: int, tokens, out=None,
+                   status=None, stream=None):
+    """Gathers and dequantises one table row per token id -> [T, cols] f32."""
+    import torch
+    op = "embedding_rows"
+    _require(table.is_cuda and table.is_contiguous(), op,
+             "table must be a contiguous CUDA tensor")
+    _require(table.numel() * table.element_size() >= vocab * row_bytes(qtype, cols),
+             op, "table smaller than vocab rows")
+    _require(tokens.is_cuda and tokens.dtype == torch.int32, op,
+             "tokens must be int32 CUDA")
+    rows = tokens.numel()
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.float32, device=tokens.device)
+    _check(load().mlb_embedding_gather(_ptr(table), qtype, vocab, cols,
+                                       _ptr(tokens), rows, _ptr(out),
+                                       _ptr(status), _stream(stream)), op)
+    return out
+
+
+def status_check(status, stream=None) -> int:
+    """Synchronises and returns the device status bits (0 = clean)."""
+    bits = ctypes.c_int32(0)
+    rc = load().mlb_status_check(_ptr(status), ctypes.byref(bits),
+                                 _stream(stream))
+    if rc not in (0, 3):
+        _check(rc, "status_check")
+    return bits.value
