@@ -144,29 +144,32 @@ class ClockSampler:
 class LayerStep:
     """Device buffers and launches of one layer-op step for `tokens` rows."""
 
-    def __init__(self, cfg, device, tokens: int, pos_offset: int):
+    def __init__(self, cfg, device, tokens: int, pos_offset: int, ops=None):
         import torch
         import mlb
         self.mlb = mlb
         self.cfg = cfg
         self.T = tokens
         self.dev = device
-        self.d = wl.make_inputs(cfg, device, tokens=tokens, pos_offset=pos_offset)
+        all_ops = ["embedding", "rmsnorm", "rope", "swiglu"]
+        if cfg.softmax_cols:
+            all_ops.append("softmax")
+        self.ops = [o for o in all_ops if ops is None or o in ops]
+        if not self.ops:
+            raise ValueError(f"no operator of {ops} in workload {cfg.name}")
+        self.d = wl.make_inputs(cfg, device, tokens=tokens, pos_offset=pos_offset,
+                                ops=self.ops)
         max_pos = (pos_offset + tokens - 1) if cfg.positions == "arange" \
             else cfg.max_position()
         self.rope_table = torch.from_numpy(
             mlb.rope_table(cfg.theta, cfg.head_dim, max_pos + 1)).to(device)
-        self.ops = ["embedding", "rmsnorm", "rope", "swiglu"]
-        if cfg.softmax_cols:
-            self.ops.append("softmax")
 
     def bytes(self):
         c, t = self.cfg, self.T
         b = {"embedding": c.bytes_embedding(t), "rmsnorm": c.bytes_rmsnorm(t),
-             "rope": c.bytes_rope(t), "swiglu": c.bytes_swiglu(t)}
-        if c.softmax_cols:
-            b["softmax"] = c.bytes_softmax(t)
-        return b
+             "rope": c.bytes_rope(t), "swiglu": c.bytes_swiglu(t),
+             "softmax": c.bytes_softmax(t)}
+        return {o: b[o] for o in self.ops}
 
     def launch(self, op, stream=None, rows=None):
         """Launches one operator over rows [r0, r1) (all rows by default)."""
@@ -461,12 +464,14 @@ def gpu_arm(args, cfg):
                                 device_id=dev)
     # weak scaling: every GPU owns a block of cfg.tokens rows (positions of a
     # sequence each); --strong splits one batch of cfg.tokens rows instead.
+    total_tokens = args.tokens or cfg.tokens
     if args.strong:
-        r0, r1 = wl.shard_range(cfg.tokens, world, rank)
+        r0, r1 = wl.shard_range(total_tokens, world, rank)
         tokens, pos_offset = r1 - r0, r0
     else:
-        tokens, pos_offset = cfg.tokens, 0
-    step = LayerStep(cfg, dev, tokens, pos_offset)
+        tokens, pos_offset = total_tokens, 0
+    ops = args.ops.split(",") if args.ops else None
+    step = LayerStep(cfg, dev, tokens, pos_offset, ops)
     nops = len(step.ops)
     op_bytes = step.bytes()
     for _ in range(args.warmup):
@@ -491,7 +496,10 @@ def gpu_arm(args, cfg):
     bits.copy_(step.d["status"])
     if int(bits.item()) != 0:
         raise RuntimeError(f"device status raised: {int(bits.item())}")
-    e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps)
+    if args.no_e2e:
+        e2e_ms, h2d, d2h = float("nan"), 0, 0
+    else:
+        e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps)
     stats = torch.tensor([total_ms, e2e_ms] + op_ms, dtype=torch.float64,
                          device=dev)
     if world > 1:
@@ -500,7 +508,7 @@ def gpu_arm(args, cfg):
     total_ms, e2e_ms, op_ms = stats[0], stats[1], stats[2:]
     clocks = sampler.summary()
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and ops is None:
         cpu = run_cpu(cfg, 3, 1, budget_s=args.cpu_budget / 2)
     if world > 1:
         dist.barrier()
@@ -541,9 +549,10 @@ def gpu_arm(args, cfg):
                      "traffic": profile_traffic(dom, cfg.name),
                      "algorithmic_bytes": op_bytes[dom]},
         "clocks": clocks,
-        "e2e": {"value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
+        "e2e": None if args.no_e2e else {
+            "value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": args.steps * sum(
             step.cfg.n_heads if o == "softmax" else 1 for o in step.ops),
     }
@@ -569,6 +578,11 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0,
                     help="seconds of CPU work for the CPU legs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ops", default="",
+                    help="comma list: time only these operators of the step")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="token rows per step instead of the workload's T")
     args = ap.parse_args()
     cfg = wl.CONFIGS[args.workload]
     if args.impl == "reference":

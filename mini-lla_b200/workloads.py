@@ -168,41 +168,51 @@ def positions_for(cfg: LayerConfig, device, tokens: Optional[int] = None,
                          dtype=torch.int32)
 
 
+ALL_OPS = ("embedding", "rmsnorm", "rope", "swiglu", "softmax")
+
+
 def make_inputs(cfg: LayerConfig, device, tokens: Optional[int] = None,
-                pos_offset: int = 0, with_softmax: bool = True):
-    """Allocates and fills every input and output buffer of one layer-op
-    step (embedding, residual RMSNorm, RoPE(+bias), SwiGLU, softmax)."""
+                pos_offset: int = 0, ops=ALL_OPS):
+    """Allocates and fills the input and output buffers of the layer-op
+    step's operators named in `ops` (embedding, residual RMSNorm,
+    RoPE(+bias), SwiGLU, softmax); buffers of other operators are None."""
     import torch
     T = cfg.tokens if tokens is None else tokens
     H, F, hd = cfg.hidden, cfg.ffn, cfg.head_dim
     s = cfg.seed
     f32 = dict(device=device, dtype=torch.float32)
-    d = {}
-    d["table"] = quant_table(cfg.qtype, cfg.vocab, H, device, s)
-    d["tokens"] = torch.randint(0, cfg.vocab, (T,), generator=_gen(device, s, 1),
-                                device=device, dtype=torch.int32)
-    d["emb_out"] = torch.empty((T, H), **f32)
-    d["x"] = torch.randn((T, H), generator=_gen(device, s, 2), **f32)
-    d["residual"] = (torch.randn((T, H), generator=_gen(device, s, 3), **f32)
-                     if cfg.residual else None)
-    d["w"] = torch.randn((H,), generator=_gen(device, s, 4), **f32) * 0.1 + 1.0
-    d["h"] = torch.empty((T, H), **f32) if cfg.residual else None
-    d["y"] = torch.empty((T, H), **f32)
-    d["gate"] = torch.randn((T, F), generator=_gen(device, s, 5), **f32)
-    d["up"] = torch.randn((T, F), generator=_gen(device, s, 6), **f32)
-    d["ffn_out"] = torch.empty((T, F), **f32)
-    d["q"] = torch.randn((T, cfg.n_heads, hd), generator=_gen(device, s, 8), **f32)
-    d["k"] = torch.randn((T, cfg.n_kv_heads, hd), generator=_gen(device, s, 9),
-                         **f32)
-    d["positions"] = positions_for(cfg, device, T, pos_offset)
-    if cfg.bias:
-        d["bq"] = torch.randn((cfg.n_heads * hd,), generator=_gen(device, s, 12),
-                              **f32) * 0.02
-        d["bk"] = torch.randn((cfg.n_kv_heads * hd,),
-                              generator=_gen(device, s, 13), **f32) * 0.02
-    else:
-        d["bq"] = d["bk"] = None
-    if with_softmax and cfg.softmax_cols:
+    d = dict.fromkeys(["table", "tokens", "emb_out", "x", "residual", "w", "h",
+                       "y", "gate", "up", "ffn_out", "q", "k", "positions",
+                       "bq", "bk", "scores", "valid_len", "probs"])
+    if "embedding" in ops:
+        d["table"] = quant_table(cfg.qtype, cfg.vocab, H, device, s)
+        d["tokens"] = torch.randint(0, cfg.vocab, (T,),
+                                    generator=_gen(device, s, 1),
+                                    device=device, dtype=torch.int32)
+        d["emb_out"] = torch.empty((T, H), **f32)
+    if "rmsnorm" in ops:
+        d["x"] = torch.randn((T, H), generator=_gen(device, s, 2), **f32)
+        if cfg.residual:
+            d["residual"] = torch.randn((T, H), generator=_gen(device, s, 3), **f32)
+            d["h"] = torch.empty((T, H), **f32)
+        d["w"] = torch.randn((H,), generator=_gen(device, s, 4), **f32) * 0.1 + 1.0
+        d["y"] = torch.empty((T, H), **f32)
+    if "swiglu" in ops:
+        d["gate"] = torch.randn((T, F), generator=_gen(device, s, 5), **f32)
+        d["up"] = torch.randn((T, F), generator=_gen(device, s, 6), **f32)
+        d["ffn_out"] = torch.empty((T, F), **f32)
+    if "rope" in ops:
+        d["q"] = torch.randn((T, cfg.n_heads, hd), generator=_gen(device, s, 8),
+                             **f32)
+        d["k"] = torch.randn((T, cfg.n_kv_heads, hd),
+                             generator=_gen(device, s, 9), **f32)
+        d["positions"] = positions_for(cfg, device, T, pos_offset)
+        if cfg.bias:
+            d["bq"] = torch.randn((cfg.n_heads * hd,),
+                                  generator=_gen(device, s, 12), **f32) * 0.02
+            d["bk"] = torch.randn((cfg.n_kv_heads * hd,),
+                                  generator=_gen(device, s, 13), **f32) * 0.02
+    if "softmax" in ops and cfg.softmax_cols:
         rows = cfg.n_heads * T
         d["scores"] = torch.randn((rows, cfg.softmax_cols),
                                   generator=_gen(device, s, 14), **f32) * 2.0
