@@ -15,7 +15,8 @@
  *     stream).  Calls are asynchronous on that stream and run on the device
  *     that is current on the calling thread; the stream must belong to it.
  *   - Return value: MLB_OK, or MLB_ERR_ARG for a rejected argument (nothing is
- *     launched), or MLB_ERR_CUDA when the launch failed.  The message of the
+ *     launched), MLB_ERR_RANGE for a host-checked id or position outside its
+ *     table (nothing is launched), or MLB_ERR_CUDA when the launch failed.  The message of the
  *     last failure on the calling thread is mlb_last_error().
  *   - Conditions only the device can see (a token id outside the table, a
  *     position outside the RoPE table, a softmax row length outside [1, cols])
@@ -44,7 +45,8 @@ enum {
   MLB_OK = 0,
   MLB_ERR_ARG = 1,
   MLB_ERR_CUDA = 2,
-  MLB_ERR_RANGE = 3 /* returned by host-side helpers that read the status */
+  MLB_ERR_RANGE = 3 /* a token id or position checked on the host is out of
+                       range, or mlb_status_check found a status bit set */
 };
 
 /* Status bits written by kernels into the optional device status word. */
@@ -128,17 +130,25 @@ int mlb_rope_table_build_host(float theta, int hd, int64_t pos_begin,
  * cuda_ops.cu:206-220, 298-308; CPU forward.cc:113-119 -> ops.cc:126-142).
  *   q: [rows, nq, hd], k: [rows, nk, hd]  (k may be NULL when nk == 0)
  *   bq: [nq*hd] or NULL, bk: [nk*hd] or NULL (added before rotation)
- *   positions: [rows] int32; cos_sin: table from mlb_rope_table_build_host
- *   with table_rows positions starting at position 0.
+ *   positions: [rows] int32 device array, or NULL for consecutive
+ *   positions: token t then sits at position_base + t (a prefill chunk, or
+ *   the single token of a decode step with rows = 1).
+ *   cos_sin: table from mlb_rope_table_build_host with table_rows positions
+ *   starting at position 0.
  *   neox = 0: pairs (2j, 2j+1); neox = 1: pairs (j, j + hd/2).
  * x0' = x0*c - x1*s, x1' = x0*s + x1*c with separate roundings: bit-exact.
- * A token whose position is outside [0, table_rows) gets its bias added but
- * is not rotated, and MLB_STATUS_BAD_POSITION is raised.
+ * With a positions array, a token whose position is outside [0, table_rows)
+ * gets its bias added but is not rotated, and MLB_STATUS_BAD_POSITION is
+ * raised.  Without one, the range [position_base, position_base + rows) is
+ * checked on the host and MLB_ERR_RANGE returned (nothing launched) if it
+ * leaves the table, as the reference throws for a negative position
+ * (ops.cc:132-134).
  */
 int mlb_rope_f32(float* q, float* k, const float* bq, const float* bk,
-                 const int32_t* positions, const float* cos_sin,
-                 int64_t table_rows, int64_t rows, int nq, int nk, int hd,
-                 int neox, int32_t* status, void* stream);
+                 const int32_t* positions, int64_t position_base,
+                 const float* cos_sin, int64_t table_rows, int64_t rows,
+                 int nq, int nk, int hd, int neox, int32_t* status,
+                 void* stream);
 
 /*
  * Row softmax over the first valid_len[r] entries of each row, zeros after
@@ -167,6 +177,16 @@ int mlb_softmax_rows_f32(const float* x, float* y, int64_t rows, int64_t cols,
 int mlb_embedding_gather(const void* table, int qtype, int64_t vocab,
                          int64_t cols, const int32_t* tokens, int64_t rows,
                          float* out, int32_t* status, void* stream);
+
+/*
+ * One embedding row for a token id held on the host: the per-token form of
+ * mlb_embedding_gather that CudaEmbeddingRow (cuda_ops.cu:264-296) maps to.
+ * The id is range-checked on the host: MLB_ERR_RANGE (nothing launched) when
+ * it is outside [0, vocab), as the reference throws std::out_of_range
+ * (cuda_ops.cu:265-267, quant.cc:279-281).  out: [cols] fp32.
+ */
+int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
+                      int64_t cols, int32_t token, float* out, void* stream);
 
 /*
  * Helper for synchronous callers: waits for `stream`, copies the device

@@ -8,16 +8,15 @@
 // Add / AddBias (ops.cc:117-124, forward.cc:36-47) are single fp32 adds and
 // bit-exact.
 //
-// All kernels are grid-stride loops over float4 with four independent
-// float4 loads per operand in flight per thread; HBM roofline 12 bytes per
-// element for the binary ops, 8 for the unary ones.
+// All kernels map one float4 (or one scalar) to one thread over a grid that
+// covers the array; HBM roofline 12 bytes per element for the binary ops, 8
+// for the unary ones.
 #include "common.cuh"
 
 namespace mlb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
 
 __device__ __forceinline__ float Silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
@@ -51,26 +50,18 @@ __device__ __forceinline__ float4 Apply4(const Op& op, const float4& a,
 }
 
 // out[i] = op(a[i], b[i]) over n4 float4s; b unused (nullptr) for unary ops.
+// One float4 per thread and a grid that covers the whole array: CTAs are
+// issued in index order, so the DRAM stream stays linear (measured 7.2 TB/s
+// on B200 for SwiGLU, against ~6.0 TB/s for a persistent grid-stride loop
+// whose stride scatters every CTA across the whole array).  The loop only
+// runs more than once for arrays beyond 2^31 CTAs.
 template <typename Op, bool BINARY>
 __global__ void __launch_bounds__(kThreads)
-    Vec4Kernel(const float4* a, const float4* b,
-               float4* out, int64_t n4) {
+    Vec4Kernel(const float4* a, const float4* b, float4* out, int64_t n4) {
   const Op op;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-    float4 va[kUnroll], vb[kUnroll];
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k) va[k] = LoadStream(a + i + k * stride);
-    if (BINARY) {
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) vb[k] = LoadStream(b + i + k * stride);
-    }
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k)
-      StoreStream(out + i + k * stride, Apply4(op, va[k], BINARY ? vb[k] : va[k]));
-  }
-  for (; i < n4; i += stride) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < n4; i += stride) {
     const float4 va = LoadStream(a + i);
     const float4 vb = BINARY ? LoadStream(b + i) : va;
     StoreStream(out + i, Apply4(op, va, vb));
@@ -115,12 +106,12 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Enough CTAs to fill every SM with 2048 resident threads, fewer for small n.
+// One thread per work item (capped at 2^31 - 1 CTAs).
 unsigned GridFor(int64_t work_items) {
-  const int64_t full = static_cast<int64_t>(SmCount()) * (2048 / kThreads);
+  const int64_t cap = 0x7fffffff;
   int64_t need = (work_items + kThreads - 1) / kThreads;
   if (need < 1) need = 1;
-  return static_cast<unsigned>(need < full ? need : full);
+  return static_cast<unsigned>(need < cap ? need : cap);
 }
 
 template <typename Op, bool BINARY>

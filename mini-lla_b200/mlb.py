@@ -40,8 +40,10 @@ SIGNATURES = {
     "mlb_rope_table_build_host": (c_int, [c_float, c_int, c_int64, c_int64,
                                           c_void_p]),
     "mlb_rope_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                             c_void_p, c_int64, c_int64, c_int, c_int, c_int,
-                             c_int, c_void_p, c_void_p]),
+                             c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
+                             c_int, c_int, c_void_p, c_void_p]),
+    "mlb_embedding_row": (c_int, [c_void_p, c_int, c_int64, c_int64, ctypes.c_int32,
+                                  c_void_p, c_void_p]),
     "mlb_softmax_rows_f32": (c_int, [c_void_p, c_void_p, c_int64, c_int64,
                                      c_void_p, c_void_p, c_void_p]),
     "mlb_embedding_gather": (c_int, [c_void_p, c_int, c_int64, c_int64,
@@ -212,8 +214,11 @@ def rope_table(theta: float, head_dim: int, positions: int, pos_begin: int = 0):
 
 
 def rope(q, k, positions, table, neox: bool, bq=None, bk=None, status=None,
-         stream=None):
-    """In-place bias add + RoPE on q [T, nq, hd] and k [T, nk, hd]."""
+         stream=None, position_base: int = 0):
+    """In-place bias add + RoPE on q [T, nq, hd] and k [T, nk, hd].
+
+    `positions` is an int32 [T] CUDA tensor, or None for consecutive
+    positions position_base + t."""
     import torch
     op = "rope"
     _f32_cuda(q, op, "q")
@@ -226,8 +231,9 @@ def rope(q, k, positions, table, neox: bool, bq=None, bk=None, status=None,
                  "k must be [tokens, kv_heads, head_dim]")
         nk = k.shape[1]
     _require(hd % 2 == 0, op, "expected [heads, even_dim]")
-    _require(positions.is_cuda and positions.dtype == torch.int32 and
-             positions.numel() == rows, op, "positions must be int32 [tokens]")
+    if positions is not None:
+        _require(positions.is_cuda and positions.dtype == torch.int32 and
+                 positions.numel() == rows, op, "positions must be int32 [tokens]")
     _f32_cuda(table, op, "table")
     _require(table.dim() == 2 and table.shape[1] == hd, op,
              "table must be [positions, head_dim]")
@@ -236,9 +242,10 @@ def rope(q, k, positions, table, neox: bool, bq=None, bk=None, status=None,
             _f32_cuda(b, op, name)
             _require(b.numel() == n * hd, op, f"{name} shape mismatch")
     _check(load().mlb_rope_f32(_ptr(q), _ptr(k), _ptr(bq), _ptr(bk),
-                               _ptr(positions), _ptr(table), table.shape[0],
-                               rows, nq, nk, hd, 1 if neox else 0,
-                               _ptr(status), _stream(stream)), op)
+                               _ptr(positions), int(position_base), _ptr(table),
+                               table.shape[0], rows, nq, nk, hd,
+                               1 if neox else 0, _ptr(status), _stream(stream)),
+           op)
 
 
 def softmax_rows(x, valid_len=None, out=None, status=None, stream=None):
@@ -276,6 +283,18 @@ def embedding_rows(table, qtype: int, vocab: int, cols: int, tokens, out=None,
     _check(load().mlb_embedding_gather(_ptr(table), qtype, vocab, cols,
                                        _ptr(tokens), rows, _ptr(out),
                                        _ptr(status), _stream(stream)), op)
+    return out
+
+
+def embedding_row(table, qtype: int, vocab: int, cols: int, token: int,
+                  out=None, stream=None):
+    """One dequantised row for a host token id -> [cols] f32 (IndexError when
+    the id is outside the table, like the reference's std::out_of_range)."""
+    import torch
+    if out is None:
+        out = torch.empty((cols,), dtype=torch.float32, device=table.device)
+    _check(load().mlb_embedding_row(_ptr(table), qtype, vocab, cols, int(token),
+                                    _ptr(out), _stream(stream)), "embedding_row")
     return out
 
 

@@ -62,10 +62,10 @@ def test_bad_arguments_rejected_on_host():
         lambda: lib.mlb_mul_f32(bogus, None, bogus, 8, None),
         lambda: lib.mlb_add_f32(bogus, bogus, None, 8, None),
         lambda: lib.mlb_add_bias_f32(None, None, bogus, 1, 8, None),
-        lambda: lib.mlb_rope_f32(bogus, bogus, None, None, bogus, bogus, 4, 1, 1,
-                                 1, 7, 0, None, None),
-        lambda: lib.mlb_rope_f32(bogus, bogus, None, None, None, bogus, 4, 1, 1,
-                                 1, 8, 0, None, None),
+        lambda: lib.mlb_rope_f32(bogus, bogus, None, None, bogus, 0, bogus, 4, 1,
+                                 1, 1, 7, 0, None, None),
+        lambda: lib.mlb_rope_f32(bogus, bogus, None, None, bogus, 0, None, 4, 1,
+                                 1, 1, 8, 0, None, None),
         lambda: lib.mlb_softmax_rows_f32(bogus, None, 1, 8, None, None, None),
         lambda: lib.mlb_softmax_rows_f32(bogus, bogus, 1, 0, None, None, None),
         lambda: lib.mlb_embedding_gather(bogus, 9, 4, 32, bogus, 1, bogus, None, None),
@@ -79,6 +79,23 @@ def test_bad_arguments_rejected_on_host():
         assert lib.mlb_last_error(), f"case {i} left no message"
 
 
+def test_host_side_range_checks():
+    """Per-token forms check the token id / position range on the host and
+    return MLB_ERR_RANGE without launching (the reference throws
+    std::out_of_range, cuda_ops.cu:265-267, and invalid_argument for a
+    negative position, ops.cc:132-134)."""
+    lib = mlb.load()
+    bogus = ctypes.c_void_p(16)
+    assert lib.mlb_embedding_row(bogus, 1, 10, 32, 10, bogus, None) == 3
+    assert lib.mlb_embedding_row(bogus, 1, 10, 32, -1, bogus, None) == 3
+    # consecutive positions [base, base + rows) must sit inside the table
+    assert lib.mlb_rope_f32(bogus, bogus, None, None, None, -1, bogus, 8, 1, 1,
+                            1, 8, 0, None, None) == 3
+    assert lib.mlb_rope_f32(bogus, bogus, None, None, None, 5, bogus, 8, 4, 1,
+                            1, 8, 0, None, None) == 3
+    assert lib.mlb_last_error()
+
+
 def test_empty_inputs_are_noops():
     """rows == 0 launches nothing and succeeds (the reference's size-0
     early returns, cuda_ops.cu:225, 235, 246, 303)."""
@@ -89,8 +106,8 @@ def test_empty_inputs_are_noops():
     assert lib.mlb_silu_f32(bogus, bogus, 0, None) == 0
     assert lib.mlb_softmax_rows_f32(bogus, bogus, 0, 8, None, None, None) == 0
     assert lib.mlb_embedding_gather(bogus, 1, 4, 32, bogus, 0, bogus, None, None) == 0
-    assert lib.mlb_rope_f32(bogus, bogus, None, None, bogus, bogus, 4, 0, 1, 1,
-                            8, 1, None, None) == 0
+    assert lib.mlb_rope_f32(bogus, bogus, None, None, bogus, 0, bogus, 4, 0, 1,
+                            1, 8, 1, None, None) == 0
 
 
 @pytest.mark.parametrize("hd,theta,begin,end", [

@@ -392,3 +392,61 @@ def test_small_configs_full_vs_oracle(cuda, oracle, name):
         assert bad == 0
         assert_rel(host(d["probs"]), want, what="softmax")
     assert mlb.status_check(d["status"]) == 0
+
+
+# ---------------------------------------------------------------- per-token forms
+
+def test_rope_consecutive_positions_without_array(cuda, oracle):
+    """positions = NULL: token t sits at position_base + t (prefill chunk);
+    rows = 1 is the reference's per-token CudaRope call."""
+    import torch
+    rng = np.random.default_rng(21)
+    for neox, base, t in ((0, 0, 40), (1, 1000, 33), (0, 2047, 1), (1, 65535, 1)):
+        q = rng.standard_normal((t, 4, 64), dtype=np.float32)
+        k = rng.standard_normal((t, 2, 64), dtype=np.float32)
+        pos = np.arange(base, base + t, dtype=np.int32)
+        wq, wk, _ = oracle.rope(q, k, pos, 1e6, neox)
+        table = dev(mlb.rope_table(1e6, 64, base + t), cuda)
+        qd, kd = dev(q, cuda), dev(k, cuda)
+        mlb.rope(qd, kd, None, table, bool(neox), position_base=base)
+        assert_bitexact(host(qd), wq, "q")
+        assert_bitexact(host(kd), wk, "k")
+    with pytest.raises(IndexError):
+        mlb.rope(qd, kd, None, table, True, position_base=base + 1)
+
+
+@pytest.mark.parametrize("qtype", [wl.F32, wl.Q8_0, wl.Q4_0, wl.Q4_1])
+def test_embedding_row_host_token(cuda, oracle, qtype):
+    vocab, cols = 50, 896
+    table = wl.numpy_quant_table(qtype, vocab, cols, seed=3)
+    td = dev(table, cuda)
+    for token in (0, 17, vocab - 1):
+        want, _ = oracle.embedding(table, qtype, vocab, cols,
+                                   np.array([token], np.int32))
+        got = mlb.embedding_row(td, qtype, vocab, cols, token)
+        assert_bitexact(host(got), want[0], f"token {token}")
+    for bad in (-1, vocab):
+        with pytest.raises(IndexError):
+            mlb.embedding_row(td, qtype, vocab, cols, bad)
+
+
+def test_large_batch_flat_grids(cuda, oracle):
+    """Flat one-item-per-thread grids over many rows: sampled rows match."""
+    import torch
+    rng = np.random.default_rng(8)
+    T, vocab, cols = 20000, 3000, 4096
+    table = wl.numpy_quant_table(wl.Q8_0, vocab, cols, seed=5)
+    tokens = rng.integers(0, vocab, T).astype(np.int32)
+    out = host(mlb.embedding_rows(dev(table, cuda), wl.Q8_0, vocab, cols,
+                                  dev(tokens, cuda)))
+    rows = np.r_[0:3, T - 3:T, rng.integers(0, T, 50)]
+    want, _ = oracle.embedding(table, wl.Q8_0, vocab, cols, tokens[rows])
+    assert_bitexact(out[rows], want, "embedding sample")
+    q = rng.standard_normal((T, 8, 128), dtype=np.float32)
+    k = rng.standard_normal((T, 2, 128), dtype=np.float32)
+    table_r = dev(mlb.rope_table(5e5, 128, T), cuda)
+    qd, kd = dev(q, cuda), dev(k, cuda)
+    mlb.rope(qd, kd, None, table_r, False)
+    wq, wk, _ = oracle.rope(q[rows], k[rows], rows.astype(np.int32), 5e5, 0)
+    assert_bitexact(host(qd)[rows], wq, "rope q sample")
+    assert_bitexact(host(kd)[rows], wk, "rope k sample")
