@@ -15,14 +15,11 @@
 // is ceil(cols/32) blocks, so rows are only 2-byte aligned in general
 // (cols = 896, Q8_0: 952 B per row).
 //
-// Vector kernels (cols % 4 == 0): each thread produces float4s of output —
-// 4 consecutive values of one block — from the block's 2-byte scale
-// (broadcast across the 8 threads of the block) and 4 quant bytes read as two
-// aligned u16 (Q8_0/Q4_0) or one u32 (Q4_1).  The flat kernel gives every
-// thread one float4 of the [rows, cols] output; the row-per-CTA kernel (for
-// more than 2^32 float4s) gives a thread NG of them, all loaded before any is
-// decoded.  Output stores are 16-byte and fully coalesced.  Scalar kernel
-// otherwise.
+// Kernels (cols % 4 == 0, 16-byte aligned output): one CTA per token row.
+// Quantised tables stage the row's bytes in shared memory with 16-byte loads
+// and decode float4s — 4 consecutive values of one block — from there; F32
+// tables copy the row with float4 loads.  Output stores are 16-byte and fully
+// coalesced.  Any other shape takes the scalar kernel (one value per thread).
 // HBM roofline per row: row_bytes read + 4 * cols written (+ 4 for the id).
 #include <climits>
 
@@ -30,6 +27,10 @@
 
 namespace mlb {
 namespace {
+
+// Largest staged row (bytes of dynamic shared memory without an opt-in):
+// Q8_0 rows up to cols ~ 45000.  Longer rows take the scalar kernel.
+constexpr int64_t kMaxStagedBytes = 48 * 1024;
 
 struct EmbArgs {
   const uint8_t* table;
@@ -47,75 +48,50 @@ __device__ __forceinline__ uint32_t LoadU16(const uint8_t* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
-// Four consecutive quant bytes starting at a 2-byte aligned address.
-__device__ __forceinline__ uint32_t Load4Bytes2(const uint8_t* p) {
-  return LoadU16(p) | (LoadU16(p + 2) << 16);
-}
-
-// Raw bytes of one output float4 (block b = o / 8, values e..e+3 with
-// e = (o % 8) * 4): the block's scale word and four quant bytes.
-struct RawGroup {
-  uint32_t scale;  // d (Q8_0, Q4_0) or d | m << 16 (Q4_1)
-  uint32_t quants; // 4 quant bytes, or the high-nibble bytes pre-shifted
-};
-
+// Decodes output float4 number o of a row (block b = o / 8, values e..e+3
+// with e = (o % 8) * 4) from the row's bytes staged in shared memory.
 template <int QT>
-__device__ __forceinline__ RawGroup LoadGroup(const uint8_t* row, int o) {
-  const int b = o >> 3;
+__device__ __forceinline__ float4 DecodeStaged(const uint8_t* row, int o) {
   const int e = (o & 7) << 2;
-  RawGroup g;
   if (QT == MLB_Q8_0) {
-    const uint8_t* blk = row + b * 34;
-    g.scale = LoadU16(blk);
-    g.quants = Load4Bytes2(blk + 2 + e);
-  } else if (QT == MLB_Q4_0) {
-    const uint8_t* blk = row + b * 18;
-    g.scale = LoadU16(blk);
-    g.quants = Load4Bytes2(blk + 2 + (e & 15));
-  } else {  // MLB_Q4_1
-    const uint8_t* blk = row + b * 20;
-    g.scale = __ldg(reinterpret_cast<const unsigned int*>(blk));
-    g.quants = __ldg(reinterpret_cast<const unsigned int*>(blk + 4 + (e & 15)));
+    const uint8_t* blk = row + (o >> 3) * 34;
+    const float d = Fp16BitsToF32(blk[0] | (blk[1] << 8));
+    const int8_t* qs = reinterpret_cast<const int8_t*>(blk + 2 + e);
+    return make_float4(__fmul_rn(d, static_cast<float>(qs[0])),
+                       __fmul_rn(d, static_cast<float>(qs[1])),
+                       __fmul_rn(d, static_cast<float>(qs[2])),
+                       __fmul_rn(d, static_cast<float>(qs[3])));
   }
-  if (QT != MLB_Q8_0 && e >= 16) g.quants >>= 4;  // high nibbles: last 16
-  return g;
+  const uint8_t* blk = row + (o >> 3) * (QT == MLB_Q4_0 ? 18 : 20);
+  const uint8_t* qs = blk + (QT == MLB_Q4_0 ? 2 : 4) + (e & 15);
+  const int shift = e >= 16 ? 4 : 0;  // last 16 values: high nibbles
+  const float d = Fp16BitsToF32(blk[0] | (blk[1] << 8));
+  const float n0 = static_cast<float>((qs[0] >> shift) & 15);
+  const float n1 = static_cast<float>((qs[1] >> shift) & 15);
+  const float n2 = static_cast<float>((qs[2] >> shift) & 15);
+  const float n3 = static_cast<float>((qs[3] >> shift) & 15);
+  if (QT == MLB_Q4_0) {
+    return make_float4(__fmul_rn(d, n0 - 8.0f), __fmul_rn(d, n1 - 8.0f),
+                       __fmul_rn(d, n2 - 8.0f), __fmul_rn(d, n3 - 8.0f));
+  }
+  const float m = Fp16BitsToF32(blk[2] | (blk[3] << 8));
+  return make_float4(__fadd_rn(__fmul_rn(d, n0), m), __fadd_rn(__fmul_rn(d, n1), m),
+                     __fadd_rn(__fmul_rn(d, n2), m), __fadd_rn(__fmul_rn(d, n3), m));
 }
 
+// Quantised tables: one CTA per token row.  The CTA first copies the row's
+// bytes into shared memory with 16-byte loads over the 16-byte-aligned window
+// that covers it (ggml rows are only 2-byte aligned: 952 B per Q8_0 row at
+// cols 896), then decodes float4s from shared memory and streams them out.
+// Bytes of the window that lie past the end of the table are never read.
+// (Measured on B200, Q8_0 [128256, 4096], 16384 tokens: 5.63 TB/s, against
+// 5.49 TB/s decoding straight from 2-byte global loads with every load of a
+// thread issued first, and 3.4-4.6 TB/s for flat or serial-loop forms.)
 template <int QT>
-__device__ __forceinline__ float4 DecodeGroup(const RawGroup& g) {
-  const uint32_t q = g.quants;
-  if (QT == MLB_Q8_0) {
-    const float d = Fp16BitsToF32(g.scale);
-    return make_float4(
-        __fmul_rn(d, static_cast<float>(static_cast<int8_t>(q & 0xffu))),
-        __fmul_rn(d, static_cast<float>(static_cast<int8_t>((q >> 8) & 0xffu))),
-        __fmul_rn(d, static_cast<float>(static_cast<int8_t>((q >> 16) & 0xffu))),
-        __fmul_rn(d, static_cast<float>(static_cast<int8_t>(q >> 24))));
-  } else if (QT == MLB_Q4_0) {
-    const float d = Fp16BitsToF32(g.scale);
-    return make_float4(
-        __fmul_rn(d, static_cast<float>(static_cast<int>(q & 15u) - 8)),
-        __fmul_rn(d, static_cast<float>(static_cast<int>((q >> 8) & 15u) - 8)),
-        __fmul_rn(d, static_cast<float>(static_cast<int>((q >> 16) & 15u) - 8)),
-        __fmul_rn(d, static_cast<float>(static_cast<int>((q >> 24) & 15u) - 8)));
-  } else {  // MLB_Q4_1
-    const float d = Fp16BitsToF32(g.scale & 0xffffu);
-    const float m = Fp16BitsToF32(g.scale >> 16);
-    return make_float4(
-        __fadd_rn(__fmul_rn(d, static_cast<float>(q & 15u)), m),
-        __fadd_rn(__fmul_rn(d, static_cast<float>((q >> 8) & 15u)), m),
-        __fadd_rn(__fmul_rn(d, static_cast<float>((q >> 16) & 15u)), m),
-        __fadd_rn(__fmul_rn(d, static_cast<float>((q >> 24) & 15u)), m));
-  }
-}
-
-// One CTA per token row.  Each thread owns NG output float4s of a chunk of
-// blockDim * NG float4s and issues every load of the chunk before decoding,
-// so a row costs one memory latency instead of NG serial ones.
-template <int QT, int NG>
-__global__ void __launch_bounds__(256) EmbeddingVecKernel(EmbArgs a) {
+__global__ void __launch_bounds__(256) EmbeddingStagedKernel(EmbArgs a,
+                                                             int64_t table_bytes) {
+  extern __shared__ __align__(16) uint8_t staged[];
   const int groups = a.cols >> 2;
-  const int chunk = blockDim.x * NG;
   for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
     const int32_t token = a.tokens != nullptr ? __ldg(a.tokens + t) : a.token;
     float4* out = reinterpret_cast<float4*>(a.out + static_cast<size_t>(t) * a.cols);
@@ -126,60 +102,40 @@ __global__ void __launch_bounds__(256) EmbeddingVecKernel(EmbArgs a) {
         StoreStream(out + o, make_float4(0.f, 0.f, 0.f, 0.f));
       continue;
     }
-    const uint8_t* row = a.table + static_cast<size_t>(token) * a.row_bytes;
-    for (int base = 0; base < groups; base += chunk) {
-      if (QT == MLB_F32) {
-        const float4* src = reinterpret_cast<const float4*>(row);
-        float4 v[NG];
-#pragma unroll
-        for (int k = 0; k < NG; ++k) {
-          const int o = base + threadIdx.x + k * blockDim.x;
-          if (o < groups) v[k] = __ldg(src + o);
-        }
-#pragma unroll
-        for (int k = 0; k < NG; ++k) {
-          const int o = base + threadIdx.x + k * blockDim.x;
-          if (o < groups) StoreStream(out + o, v[k]);
-        }
+    const int64_t start = static_cast<int64_t>(token) * a.row_bytes;
+    const int64_t window = start & ~int64_t{15};
+    const int chunks = static_cast<int>((start + a.row_bytes - window + 15) >> 4);
+    __syncthreads();  // the previous row's decode is done with `staged`
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      const int64_t off = window + 16 * static_cast<int64_t>(c);
+      if (off + 16 <= table_bytes) {
+        *reinterpret_cast<uint4*>(staged + 16 * c) =
+            __ldg(reinterpret_cast<const uint4*>(a.table + off));
       } else {
-        RawGroup g[NG];
-#pragma unroll
-        for (int k = 0; k < NG; ++k) {
-          const int o = base + threadIdx.x + k * blockDim.x;
-          if (o < groups) g[k] = LoadGroup<QT>(row, o);
-        }
-#pragma unroll
-        for (int k = 0; k < NG; ++k) {
-          const int o = base + threadIdx.x + k * blockDim.x;
-          if (o < groups) StoreStream(out + o, DecodeGroup<QT>(g[k]));
-        }
+        for (int b = 0; b < 16; ++b)
+          staged[16 * c + b] = off + b < table_bytes ? a.table[off + b] : 0;
       }
     }
+    __syncthreads();
+    const uint8_t* row = staged + (start - window);
+    for (int o = threadIdx.x; o < groups; o += blockDim.x)
+      StoreStream(out + o, DecodeStaged<QT>(row, o));
   }
 }
 
-// Flat form: one output float4 per thread over rows * cols/4 items, so the
-// output stream is written in address order by consecutive CTAs.  Used while
-// the item count fits 32 bits; the row-per-CTA kernel above covers the rest.
-template <int QT>
-__global__ void __launch_bounds__(256)
-    EmbeddingFlatKernel(EmbArgs a, uint32_t groups, uint32_t total) {
-  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= total) return;
-  const uint32_t t = idx / groups;
-  const int o = static_cast<int>(idx - t * groups);
-  const int32_t token = a.tokens != nullptr ? __ldg(a.tokens + t) : a.token;
-  float4* out = reinterpret_cast<float4*>(a.out) + idx;
-  if (token < 0 || token >= a.vocab) {
-    if (o == 0 && a.status != nullptr) atomicOr(a.status, MLB_STATUS_BAD_TOKEN);
-    StoreStream(out, make_float4(0.f, 0.f, 0.f, 0.f));
-    return;
-  }
-  const uint8_t* row = a.table + static_cast<size_t>(token) * a.row_bytes;
-  if (QT == MLB_F32) {
-    StoreStream(out, __ldg(reinterpret_cast<const float4*>(row) + o));
-  } else {
-    StoreStream(out, DecodeGroup<QT>(LoadGroup<QT>(row, o)));
+// F32 tables with 16-byte aligned rows: a plain row copy, one CTA per token.
+__global__ void __launch_bounds__(256) EmbeddingF32Kernel(EmbArgs a) {
+  const int groups = a.cols >> 2;
+  for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
+    const int32_t token = a.tokens != nullptr ? __ldg(a.tokens + t) : a.token;
+    float4* out = reinterpret_cast<float4*>(a.out + static_cast<size_t>(t) * a.cols);
+    const bool ok = token >= 0 && token < a.vocab;
+    if (!ok && threadIdx.x == 0 && a.status != nullptr)
+      atomicOr(a.status, MLB_STATUS_BAD_TOKEN);
+    const float4* src = reinterpret_cast<const float4*>(
+        a.table + static_cast<size_t>(ok ? token : 0) * a.row_bytes);
+    for (int o = threadIdx.x; o < groups; o += blockDim.x)
+      StoreStream(out + o, ok ? __ldg(src + o) : make_float4(0.f, 0.f, 0.f, 0.f));
   }
 }
 
@@ -250,35 +206,25 @@ int LaunchEmbedding(const void* table, int qtype, int64_t vocab, int64_t cols,
   int threads = groups < 256 ? (groups + 31) / 32 * 32 : 256;
   if (threads < 32) threads = 32;
   cudaStream_t s = AsStream(stream);
-  const bool vec = (cols % 4) == 0 && Aligned16(out) &&
-                   (qtype != MLB_F32 || (tbl & 15u) == 0);
-  const int64_t total = rows * static_cast<int64_t>(groups);
-  if (vec && total <= 0xffffffffLL - 256) {
-    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
-    const uint32_t g32 = static_cast<uint32_t>(groups);
-    const uint32_t t32 = static_cast<uint32_t>(total);
+  const int64_t row_bytes = a.row_bytes;
+  const bool vec = (cols % 4) == 0 && Aligned16(out);
+  // staged window: up to 15 leading bytes + the row, rounded to 16
+  const int64_t smem = (row_bytes + 15 + 15) / 16 * 16;
+  if (vec && qtype == MLB_F32 && (tbl & 15u) == 0) {
+    EmbeddingF32Kernel<<<grid, threads, 0, s>>>(a);
+  } else if (vec && qtype != MLB_F32 && smem <= kMaxStagedBytes) {
+    const int64_t table_bytes = vocab * row_bytes;
+    const size_t shm = static_cast<size_t>(smem);
     switch (qtype) {
-      case MLB_F32: EmbeddingFlatKernel<MLB_F32><<<blocks, 256, 0, s>>>(a, g32, t32); break;
-      case MLB_Q8_0: EmbeddingFlatKernel<MLB_Q8_0><<<blocks, 256, 0, s>>>(a, g32, t32); break;
-      case MLB_Q4_0: EmbeddingFlatKernel<MLB_Q4_0><<<blocks, 256, 0, s>>>(a, g32, t32); break;
-      case MLB_Q4_1: EmbeddingFlatKernel<MLB_Q4_1><<<blocks, 256, 0, s>>>(a, g32, t32); break;
-    }
-  } else if (vec) {
-    int ng = (groups + threads - 1) / threads;
-    if (ng > 8) ng = 8;
-    switch (ng) {
-#define MLB_NG(N)                                                            \
-  case N:                                                                    \
-    switch (qtype) {                                                         \
-      case MLB_F32: EmbeddingVecKernel<MLB_F32, N><<<grid, threads, 0, s>>>(a); break;  \
-      case MLB_Q8_0: EmbeddingVecKernel<MLB_Q8_0, N><<<grid, threads, 0, s>>>(a); break; \
-      case MLB_Q4_0: EmbeddingVecKernel<MLB_Q4_0, N><<<grid, threads, 0, s>>>(a); break; \
-      case MLB_Q4_1: EmbeddingVecKernel<MLB_Q4_1, N><<<grid, threads, 0, s>>>(a); break; \
-    }                                                                        \
-    break;
-      MLB_NG(1) MLB_NG(2) MLB_NG(3) MLB_NG(4) MLB_NG(5) MLB_NG(6) MLB_NG(7)
-      MLB_NG(8)
-#undef MLB_NG
+      case MLB_Q8_0:
+        EmbeddingStagedKernel<MLB_Q8_0><<<grid, threads, shm, s>>>(a, table_bytes);
+        break;
+      case MLB_Q4_0:
+        EmbeddingStagedKernel<MLB_Q4_0><<<grid, threads, shm, s>>>(a, table_bytes);
+        break;
+      case MLB_Q4_1:
+        EmbeddingStagedKernel<MLB_Q4_1><<<grid, threads, shm, s>>>(a, table_bytes);
+        break;
     }
   } else {
     EmbeddingScalarKernel<<<grid, 256, 0, s>>>(a, qtype);

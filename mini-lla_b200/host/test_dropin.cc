@@ -1,0 +1,334 @@
+// Drop-in check of the C++ operator layer: mini-lla's own GPU API
+// (cuda_ops.h, cuda_tensor.h, cuda_runtime.h of the reference), served by
+// this library's cuda_ops.cc / cuda_runtime.cc over libmlb.so, compared with
+// the reference's CPU operators (ops.cc, quant.cc) on the same inputs.
+//
+// Built by `make -C oracle dropin` against the reference's headers and CPU
+// sources; prints one line per failed check and exits non-zero on failure.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "mini_llama/cuda_layer_ops.h"
+#include "mini_llama/cuda_ops.h"
+#include "mini_llama/ops.h"
+#include "mini_llama/quant.h"
+
+using namespace mini_lla;
+
+namespace {
+
+int g_failures = 0;
+int g_checks = 0;
+
+void Expect(bool ok, const std::string& what) {
+  ++g_checks;
+  if (!ok) {
+    ++g_failures;
+    std::printf("FAIL: %s\n", what.c_str());
+  }
+}
+
+bool BitEqual(const std::vector<float>& a, const std::vector<float>& b) {
+  if (a.size() != b.size()) return false;
+  for (size_t i = 0; i < a.size(); ++i) {
+    if (std::isnan(a[i]) && std::isnan(b[i])) continue;
+    uint32_t x, y;
+    std::memcpy(&x, &a[i], 4);
+    std::memcpy(&y, &b[i], 4);
+    if (x != y) return false;
+  }
+  return true;
+}
+
+double MaxRel(const std::vector<float>& got, const std::vector<float>& want) {
+  if (got.size() != want.size()) return 1e30;
+  double worst = 0;
+  for (size_t i = 0; i < got.size(); ++i) {
+    if (got[i] == want[i]) continue;
+    worst = std::max(worst, std::fabs(double(got[i]) - want[i]) / std::fabs(double(want[i])));
+  }
+  return worst;
+}
+
+Tensor Random(std::vector<int> shape, std::mt19937& rng, float scale = 1.0f,
+              float shift = 0.0f) {
+  Tensor t(shape);
+  std::normal_distribution<float> n(0.0f, 1.0f);
+  for (float& v : t.data) v = n(rng) * scale + shift;
+  return t;
+}
+
+// A norm/bias vector uploaded the way UploadVector does (cuda_weights.cc:65-77).
+CudaWeight VectorWeight(const Tensor& t) {
+  CudaWeight w;
+  w.type = QuantType::kF32;
+  w.rows = static_cast<int>(t.Size());
+  w.cols = 1;
+  w.linear = false;
+  w.buffer.Reset(t.Size() * sizeof(float));
+  w.buffer.Upload(t.data.data(), t.Size() * sizeof(float));
+  return w;
+}
+
+// A table uploaded as raw blocks the way UploadQuantized does
+// (cuda_weights.cc:33-62).
+CudaWeight TableWeight(const QuantizedTensor& q) {
+  CudaWeight w;
+  w.type = q.type;
+  w.rows = q.rows;
+  w.cols = q.cols;
+  const size_t bytes = QuantizedBytes(q);
+  w.buffer.Reset(bytes);
+  const void* src = q.type == QuantType::kF32 ? static_cast<const void*>(q.f32.data.data())
+                    : q.type == QuantType::kQ8_0 ? static_cast<const void*>(q.q8_0.data())
+                    : q.type == QuantType::kQ4_0 ? static_cast<const void*>(q.q4_0.data())
+                                                 : static_cast<const void*>(q.q4_1.data());
+  w.buffer.Upload(src, bytes);
+  return w;
+}
+
+template <typename F>
+bool Throws(F&& f) {
+  try {
+    f();
+  } catch (const std::exception&) {
+    return true;
+  }
+  return false;
+}
+
+void TestPerVectorOps(std::mt19937& rng) {
+  for (int n : {3, 896, 4096, 3584, 37}) {
+    const Tensor x = Random({n}, rng);
+    const Tensor w = Random({n}, rng, 0.1f, 1.0f);
+    const CudaWeight dw = VectorWeight(w);
+    const CudaTensor dx = CudaTensor::FromHost(x);
+    const Tensor y = CudaRmsNorm(dx, dw, 1e-5f).Download();
+    Expect(MaxRel(y.data, RmsNorm(x, w, 1e-5f).data) <= 1e-5,
+           "CudaRmsNorm n=" + std::to_string(n));
+    const Tensor b = Random({n}, rng);
+    const CudaTensor db = CudaTensor::FromHost(b);
+    Expect(BitEqual(CudaAdd(dx, db).Download().data, Add(x, b).data),
+           "CudaAdd n=" + std::to_string(n));
+    Expect(MaxRel(CudaSilu(dx).Download().data, Silu(x).data) <= 1e-5,
+           "CudaSilu n=" + std::to_string(n));
+    Expect(MaxRel(CudaMul(CudaSilu(dx), db).Download().data, SwiGlu(x, b).data) <= 1e-5,
+           "CudaSilu+CudaMul n=" + std::to_string(n));
+    Expect(MaxRel(CudaSoftmax(dx).Download().data, Softmax(x).data) <= 1e-5,
+           "CudaSoftmax n=" + std::to_string(n));
+    Tensor biased = x;
+    for (size_t i = 0; i < biased.Size(); ++i) biased.data[i] += b.data[i];
+    const CudaWeight dbias = VectorWeight(b);
+    Expect(BitEqual(CudaAddBias(dx, &dbias).Download().data, biased.data),
+           "CudaAddBias n=" + std::to_string(n));
+    Expect(BitEqual(CudaAddBias(dx, nullptr).Download().data, x.data),
+           "CudaAddBias(null) n=" + std::to_string(n));
+  }
+  // reference tests/test_ops.cc:41 through the GPU path
+  Tensor x({3});
+  x.data = {1, 2, 3};
+  const CudaWeight ones = VectorWeight(Tensor({3}, 1.0f));
+  const float y0 = CudaRmsNorm(CudaTensor::FromHost(x), ones, 1e-5f).Download().data[0];
+  Expect(std::fabs(y0 - 0.46291f) <= 1e-4, "CudaRmsNorm [1,2,3] constant");
+  // error behaviour of cuda_ops.cu:196, 232, 243, 255
+  const CudaTensor d3 = CudaTensor::FromHost(x);
+  const CudaTensor d2 = CudaTensor::FromHost(Tensor({2}));
+  Expect(Throws([&] { CudaRmsNorm(d2, ones, 1e-5f); }), "CudaRmsNorm mismatch throws");
+  Expect(Throws([&] { CudaMul(d3, d2); }), "CudaMul mismatch throws");
+  Expect(Throws([&] { CudaAdd(d3, d2); }), "CudaAdd mismatch throws");
+  Expect(Throws([&] { CudaSoftmax(CudaTensor({2, 2})); }), "CudaSoftmax rank throws");
+}
+
+void TestRope(std::mt19937& rng) {
+  struct Case { int nq, nk, hd; float theta; RopeType type; };
+  const Case cases[] = {{14, 2, 64, 1e6f, RopeType::kNeoX},
+                        {32, 8, 128, 5e5f, RopeType::kNormal},
+                        {32, 32, 128, 1e4f, RopeType::kNormal},
+                        {28, 4, 128, 1e6f, RopeType::kNeoX},
+                        {3, 1, 6, 1e4f, RopeType::kNormal}};
+  for (const Case& c : cases) {
+    for (int position : {0, 1, 255, 2047, 16383, 65535}) {
+      Tensor q = Random({c.nq, c.hd}, rng);
+      Tensor k = Random({c.nk, c.hd}, rng);
+      CudaTensor dq = CudaTensor::FromHost(q.Reshape({c.nq * c.hd}));
+      CudaTensor dk = CudaTensor::FromHost(k.Reshape({c.nk * c.hd}));
+      Rope(q, k, position, c.theta, c.type);
+      CudaRope(&dq, &dk, position, c.theta, c.nq, c.nk, c.hd, c.type);
+      Expect(BitEqual(dq.Download().data, q.data) && BitEqual(dk.Download().data, k.data),
+             "CudaRope hd=" + std::to_string(c.hd) + " pos=" + std::to_string(position));
+    }
+  }
+  // test_ops.cc:65-82 constants
+  for (RopeType type : {RopeType::kNormal, RopeType::kNeoX}) {
+    Tensor host({2});
+    host.data = {1.0f, 0.0f};
+    CudaTensor dq = CudaTensor::FromHost(host);
+    CudaTensor dk = CudaTensor::FromHost(host);
+    CudaRope(&dq, &dk, 1, 10000.0f, 1, 1, 2, type);
+    const Tensor r = dq.Download();
+    Expect(std::fabs(r.data[0] - std::cos(1.0f)) <= 1e-5 &&
+               std::fabs(r.data[1] - std::sin(1.0f)) <= 1e-5,
+           "CudaRope rotates by 1 rad");
+  }
+  CudaTensor dq({8}), dk({8});
+  Expect(Throws([&] { CudaRope(&dq, &dk, -1, 1e4f, 1, 1, 8, RopeType::kNormal); }),
+         "CudaRope negative position throws");
+  Expect(Throws([&] { CudaRope(nullptr, &dk, 0, 1e4f, 1, 1, 8, RopeType::kNormal); }),
+         "CudaRope null throws");
+  Expect(CudaRopeTableRows(1e6f, 64) >= 65536, "RoPE table grown and cached");
+}
+
+void TestEmbedding(std::mt19937& rng) {
+  for (QuantType type : {QuantType::kF32, QuantType::kQ8_0, QuantType::kQ4_0,
+                         QuantType::kQ4_1}) {
+    for (int cols : {896, 4096, 40, 38}) {
+      const int vocab = 64;
+      const Tensor values = Random({vocab, cols}, rng);
+      const QuantizedTensor table = Quantize(values, type);
+      const CudaWeight dt = TableWeight(table);
+      std::vector<float> want(cols);
+      for (int token : {0, 1, 31, vocab - 1}) {
+        DequantizeRow(table, token, want.data());
+        Expect(BitEqual(CudaEmbeddingRow(dt, token).Download().data, want),
+               std::string("CudaEmbeddingRow ") + QuantTypeName(type) +
+                   " cols=" + std::to_string(cols));
+      }
+      Expect(Throws([&] { CudaEmbeddingRow(dt, vocab); }) &&
+                 Throws([&] { CudaEmbeddingRow(dt, -1); }),
+             "CudaEmbeddingRow out of range throws");
+      std::vector<int> tokens = {5, 0, 63, 5, 17};
+      const Tensor rows = CudaEmbeddingRows(dt, tokens).Download();
+      bool ok = true;
+      for (size_t r = 0; r < tokens.size(); ++r) {
+        DequantizeRow(table, tokens[r], want.data());
+        std::vector<float> got(rows.data.begin() + r * cols,
+                               rows.data.begin() + (r + 1) * cols);
+        ok = ok && BitEqual(got, want);
+      }
+      Expect(ok, std::string("CudaEmbeddingRows ") + QuantTypeName(type));
+    }
+  }
+}
+
+void TestBatched(std::mt19937& rng) {
+  const int rows = 33, cols = 4096;
+  const Tensor x = Random({rows, cols}, rng);
+  const Tensor r = Random({rows, cols}, rng);
+  const Tensor w = Random({cols}, rng, 0.1f, 1.0f);
+  const CudaWeight dw = VectorWeight(w);
+  const CudaTensor dx = CudaTensor::FromHost(x);
+  const CudaTensor dr = CudaTensor::FromHost(r);
+  CudaTensor dh;
+  const Tensor y = CudaAddRmsNormRows(dx, &dr, dw, 1e-5f, &dh).Download();
+  const Tensor h = dh.Download();
+  bool h_ok = true, y_ok = true;
+  for (int i = 0; i < rows; ++i) {
+    Tensor xi({cols}), ri({cols});
+    std::copy(x.data.begin() + i * cols, x.data.begin() + (i + 1) * cols, xi.data.begin());
+    std::copy(r.data.begin() + i * cols, r.data.begin() + (i + 1) * cols, ri.data.begin());
+    const Tensor hi = Add(xi, ri);
+    const Tensor yi = RmsNorm(hi, w, 1e-5f);
+    h_ok = h_ok && BitEqual(std::vector<float>(h.data.begin() + i * cols, h.data.begin() + (i + 1) * cols), hi.data);
+    y_ok = y_ok && MaxRel(std::vector<float>(y.data.begin() + i * cols, y.data.begin() + (i + 1) * cols), yi.data) <= 1e-5;
+  }
+  Expect(h_ok, "CudaAddRmsNormRows residual sum bit-exact");
+  Expect(y_ok, "CudaAddRmsNormRows within 1e-5");
+
+  const Tensor g = Random({rows, 14336}, rng, 3.0f);
+  const Tensor u = Random({rows, 14336}, rng);
+  Expect(MaxRel(CudaSwiGlu(CudaTensor::FromHost(g), CudaTensor::FromHost(u)).Download().data,
+                SwiGlu(g, u).data) <= 1e-5,
+         "CudaSwiGlu within 1e-5");
+
+  const int nq = 28, nk = 4, hd = 128;
+  Tensor q = Random({rows, nq * hd}, rng);
+  Tensor k = Random({rows, nk * hd}, rng);
+  const Tensor bq = Random({nq * hd}, rng, 0.02f);
+  const Tensor bk = Random({nk * hd}, rng, 0.02f);
+  const CudaWeight dbq = VectorWeight(bq), dbk = VectorWeight(bk);
+  for (bool consecutive : {true, false}) {
+    std::vector<int> positions(rows);
+    for (int i = 0; i < rows; ++i) positions[i] = consecutive ? 1000 + i : (i * 7919) % 65536;
+    CudaTensor dq = CudaTensor::FromHost(q), dk = CudaTensor::FromHost(k);
+    CudaRopeRows(&dq, &dk, &dbq, &dbk, positions, 1e6f, nq, nk, hd, RopeType::kNeoX);
+    const Tensor gq = dq.Download(), gk = dk.Download();
+    bool ok = true;
+    for (int i = 0; i < rows; ++i) {
+      Tensor qi({nq, hd}), ki({nk, hd});
+      for (int j = 0; j < nq * hd; ++j) qi.data[j] = q.data[i * nq * hd + j] + bq.data[j];
+      for (int j = 0; j < nk * hd; ++j) ki.data[j] = k.data[i * nk * hd + j] + bk.data[j];
+      Rope(qi, ki, positions[i], 1e6f, RopeType::kNeoX);
+      ok = ok && BitEqual(std::vector<float>(gq.data.begin() + i * nq * hd, gq.data.begin() + (i + 1) * nq * hd), qi.data) &&
+           BitEqual(std::vector<float>(gk.data.begin() + i * nk * hd, gk.data.begin() + (i + 1) * nk * hd), ki.data);
+    }
+    Expect(ok, consecutive ? "CudaRopeRows consecutive positions bit-exact"
+                           : "CudaRopeRows scattered positions bit-exact");
+  }
+
+  const Tensor s = Random({rows, 256}, rng, 2.0f);
+  std::vector<int> lengths(rows);
+  for (int i = 0; i < rows; ++i) lengths[i] = i * 7 % 256 + 1;
+  const Tensor p = CudaSoftmaxRows(CudaTensor::FromHost(s), &lengths).Download();
+  bool ok = true;
+  for (int i = 0; i < rows; ++i) {
+    Tensor vis({lengths[i]});
+    std::copy(s.data.begin() + i * 256, s.data.begin() + i * 256 + lengths[i], vis.data.begin());
+    const Tensor want = Softmax(vis);
+    std::vector<float> got(p.data.begin() + i * 256, p.data.begin() + i * 256 + lengths[i]);
+    ok = ok && MaxRel(got, want.data) <= 1e-5;
+    for (int j = lengths[i]; j < 256; ++j) ok = ok && p.data[i * 256 + j] == 0.0f;
+  }
+  Expect(ok, "CudaSoftmaxRows causal rows within 1e-5");
+}
+
+void TestRuntime() {
+  int device = 0;
+  cudaGetDevice(&device);
+  const size_t before = CudaPoolCachedBytes(device);
+  {
+    CudaTensor a({1 << 20});
+    CudaTensor b({1 << 20});
+  }
+  Expect(CudaPoolCachedBytes(device) >= before + (size_t{8} << 20),
+         "pool keeps freed blocks");
+  const size_t cached = CudaPoolCachedBytes(device);
+  { CudaTensor c({1 << 20}); }
+  Expect(CudaPoolCachedBytes(device) == cached, "pool reuses a freed block");
+  // large transfers go through pinned staging and round-trip exactly
+  std::vector<float> big(5 << 20);
+  for (size_t i = 0; i < big.size(); ++i) big[i] = static_cast<float>(i) * 0.5f;
+  Tensor host({static_cast<int>(big.size())});
+  host.data = big;
+  Expect(BitEqual(CudaTensor::FromHost(host).Download().data, big),
+         "staged upload/download round trip");
+  CudaPoolRelease(device);
+  Expect(CudaPoolCachedBytes(device) == 0, "pool release");
+  Expect(Throws([] { CudaSetDevice(1 << 20); }), "bad device index throws");
+}
+
+}  // namespace
+
+int main() {
+  std::mt19937 rng(20261201);
+  try {
+    TestPerVectorOps(rng);
+    TestRope(rng);
+    TestEmbedding(rng);
+    TestBatched(rng);
+    TestRuntime();
+  } catch (const std::exception& e) {
+    std::printf("FAIL: unexpected exception: %s\n", e.what());
+    return 2;
+  }
+  std::printf("%s: %d checks, %d failures\n", g_failures ? "dropin FAILED" : "dropin ok",
+              g_checks, g_failures);
+  return g_failures == 0 ? 0 : 1;
+}

@@ -1,0 +1,56 @@
+"""The reference-facing C++ layer (mini-lla_b200/host): mini-lla's own
+GPU operator API served by libmlb.so.
+
+- CPU: the reference's unchanged src/cuda_forward.cc, compiled against the
+  reference headers, needs exactly the cuda_ops.h symbols this layer's
+  cuda_ops.cc defines (link surface of the drop-in).
+- GPU: oracle/_ref/mlb_dropin_test runs the reference API (CudaRmsNorm,
+  CudaRope, CudaEmbeddingRow, ... and the row-batched additions) against the
+  reference's CPU operators.
+Both binaries are built by `make -C oracle dropin` where the reference
+headers are present; the tests skip when they were not built.
+"""
+import os
+import subprocess
+
+import pytest
+
+from conftest import ORACLE_DIR
+
+REF = os.path.join(ORACLE_DIR, "_ref")
+
+
+def test_cuda_forward_links_against_this_layer():
+    fwd = os.path.join(REF, "cuda_forward.o")
+    ops = os.path.join(REF, "cuda_ops_host.o")
+    if not (os.path.exists(fwd) and os.path.exists(ops)):
+        pytest.skip("drop-in objects not built (reference headers absent)")
+    undefined = subprocess.run(["nm", "-C", "--undefined-only", fwd], check=True,
+                               capture_output=True, text=True).stdout
+    needed = {l.split("U ", 1)[1].strip() for l in undefined.splitlines()
+              if "U mini_lla::Cuda" in l}
+    defined = subprocess.run(["nm", "-C", "--defined-only", ops], check=True,
+                             capture_output=True, text=True).stdout
+    have = {l.split(" ", 2)[2].strip() for l in defined.splitlines()
+            if " T mini_lla::Cuda" in l}
+    # the operator entry points cuda_forward.cc calls (cuda_ops.h:11-34)
+    ops_needed = {n for n in needed if n.split("(")[0] in {
+        "mini_lla::CudaRmsNorm", "mini_lla::CudaRope", "mini_lla::CudaSilu",
+        "mini_lla::CudaMul", "mini_lla::CudaAdd", "mini_lla::CudaSoftmax",
+        "mini_lla::CudaEmbeddingRow", "mini_lla::CudaAddBias"}}
+    assert len(ops_needed) >= 6, needed
+    missing = ops_needed - have
+    assert not missing, f"cuda_ops.cc lacks {missing}"
+
+
+@pytest.mark.gpu
+def test_reference_api_dropin_binary():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    exe = os.path.join(REF, "mlb_dropin_test")
+    if not os.path.exists(exe):
+        pytest.skip("mlb_dropin_test not built (reference headers absent)")
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "dropin ok" in res.stdout

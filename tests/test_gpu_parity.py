@@ -450,3 +450,16 @@ def test_large_batch_flat_grids(cuda, oracle):
     wq, wk, _ = oracle.rope(q[rows], k[rows], rows.astype(np.int32), 5e5, 0)
     assert_bitexact(host(qd)[rows], wq, "rope q sample")
     assert_bitexact(host(kd)[rows], wk, "rope k sample")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0, wl.Q4_1])
+def test_embedding_last_row_at_unaligned_table_end(cuda, oracle, qtype):
+    """The staged 16-byte window of the last row would run past a table
+    whose size is not a multiple of 16; those bytes are never read."""
+    for vocab, cols in ((3, 896), (1, 40), (5, 36)):
+        table = wl.numpy_quant_table(qtype, vocab, cols, seed=vocab)
+        tokens = np.array([vocab - 1, 0, vocab - 1], np.int32)
+        want, _ = oracle.embedding(table, qtype, vocab, cols, tokens)
+        got = mlb.embedding_rows(dev(table, cuda), qtype, vocab, cols,
+                                 dev(tokens, cuda))
+        assert_bitexact(host(got), want, f"{wl.QNAME[qtype]} vocab={vocab}")
