@@ -292,16 +292,22 @@ void TestBatched(std::mt19937& rng) {
 void TestRuntime() {
   int device = 0;
   cudaGetDevice(&device);
+  // 22 MiB blocks (a size no other check allocates)
+  const int n = (21 << 18) + 1;
   const size_t before = CudaPoolCachedBytes(device);
   {
-    CudaTensor a({1 << 20});
-    CudaTensor b({1 << 20});
+    CudaTensor a({n});
+    CudaTensor b({n});
   }
-  Expect(CudaPoolCachedBytes(device) >= before + (size_t{8} << 20),
+  Expect(CudaPoolCachedBytes(device) == before + (size_t{44} << 20),
          "pool keeps freed blocks");
   const size_t cached = CudaPoolCachedBytes(device);
-  { CudaTensor c({1 << 20}); }
-  Expect(CudaPoolCachedBytes(device) == cached, "pool reuses a freed block");
+  {
+    CudaTensor c({n});
+    Expect(CudaPoolCachedBytes(device) == cached - (size_t{22} << 20),
+           "pool reuses a freed block");
+  }
+  Expect(CudaPoolCachedBytes(device) == cached, "pool takes the block back");
   // large transfers go through pinned staging and round-trip exactly
   std::vector<float> big(5 << 20);
   for (size_t i = 0; i < big.size(); ++i) big[i] = static_cast<float>(i) * 0.5f;
