@@ -7,11 +7,15 @@
 // sources; prints one line per failed check and exits non-zero on failure.
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <random>
+#include <thread>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -320,6 +324,75 @@ void TestRuntime() {
   Expect(Throws([] { CudaSetDevice(1 << 20); }), "bad device index throws");
 }
 
+// One host thread per "device" entry; a single-GPU box lists device 0 twice
+// (independent token ranges, no waits between them).
+void TestShardingAndWaits(std::mt19937& rng) {
+  const int vocab = 100, cols = 896, total = 1001;
+  const QuantizedTensor table = Quantize(Random({vocab, cols}, rng), QuantType::kQ8_0);
+  std::vector<int> tokens(total);
+  for (int i = 0; i < total; ++i) tokens[i] = (i * 37) % vocab;
+  const std::vector<int> devices = {0, 0, 0};
+  std::vector<std::vector<float>> parts(devices.size());
+  std::vector<std::pair<int, int>> ranges(devices.size());
+  std::mutex m;
+  CudaShardRows(total, devices, [&](int, int begin, int end) {
+    const CudaWeight dt = TableWeight(table);  // replicated per shard
+    std::vector<int> mine(tokens.begin() + begin, tokens.begin() + end);
+    const Tensor out = CudaEmbeddingRows(dt, mine).Download();
+    std::lock_guard<std::mutex> lock(m);
+    const size_t slot = begin == 0 ? 0 : (end == total ? devices.size() - 1 : 1);
+    parts[slot] = out.data;
+    ranges[slot] = {begin, end};
+  });
+  bool ok = ranges[0].first == 0 && ranges.back().second == total;
+  std::vector<float> want(cols);
+  for (size_t s = 0; s < parts.size(); ++s) {
+    if (s > 0) ok = ok && ranges[s].first == ranges[s - 1].second;
+    for (int r = ranges[s].first; r < ranges[s].second; ++r) {
+      DequantizeRow(table, tokens[r], want.data());
+      const size_t off = static_cast<size_t>(r - ranges[s].first) * cols;
+      ok = ok && BitEqual(std::vector<float>(parts[s].begin() + off,
+                                             parts[s].begin() + off + cols), want);
+    }
+  }
+  Expect(ok, "CudaShardRows: contiguous ranges, gathered rows bit-exact");
+  Expect(ShardRange(10, 3, 0) == std::make_pair(0, 4) &&
+             ShardRange(10, 3, 2) == std::make_pair(7, 10),
+         "ShardRange remainder rule");
+  // A failing shard: every thread is joined and the first error surfaces.
+  std::atomic<int> finished{0};
+  const bool rethrown = Throws([&] {
+    CudaShardRows(30, devices, [&](int, int begin, int) {
+      if (begin == 10) throw std::runtime_error("injected shard failure");
+      finished.fetch_add(1);
+    });
+  });
+  Expect(rethrown && finished.load() == 2, "CudaShardRows rethrows after join");
+
+  // Bounded wait: the stream is held by a host function (no GPU work is
+  // stalled), the wait times out and returns false, then succeeds once the
+  // host releases the stream.
+  cudaStream_t stream;
+  cudaEvent_t event;
+  cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+  cudaEventCreateWithFlags(&event, cudaEventDisableTiming);
+  static std::atomic<bool> release{false};
+  release.store(false);
+  cudaLaunchHostFunc(stream, [](void*) {
+    for (int i = 0; i < 20000 && !release.load(); ++i) {
+      std::this_thread::sleep_for(std::chrono::microseconds(250));
+    }
+  }, nullptr);
+  cudaEventRecord(event, stream);
+  const bool early = CudaWaitEvent(event, 50.0);
+  release.store(true);
+  const bool late = CudaWaitEvent(event, 10000.0);
+  Expect(!early && late, "CudaWaitEvent times out, then completes");
+  cudaStreamSynchronize(stream);
+  cudaEventDestroy(event);
+  cudaStreamDestroy(stream);
+}
+
 }  // namespace
 
 int main() {
@@ -329,6 +402,7 @@ int main() {
     TestRope(rng);
     TestEmbedding(rng);
     TestBatched(rng);
+    TestShardingAndWaits(rng);
     TestRuntime();
   } catch (const std::exception& e) {
     std::printf("FAIL: unexpected exception: %s\n", e.what());
