@@ -292,6 +292,65 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
     return ms, h2d, d2h
 
 
+GRAPH_REPEAT = 10
+
+
+def graph_timing(step: LayerStep, args, world):
+    """Latency-bound batches: the step's launches are captured once in a CUDA
+    graph (GRAPH_REPEAT steps per graph, so graph-launch overhead is
+    amortised) and replayed; per-operator times come from graphs holding
+    GRAPH_REPEAT launches of that operator alone.  Returns total ms over
+    args.steps steps, per-op ms, and the clock sampler."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()  # warm the capture stream once outside the graph
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(GRAPH_REPEAT):
+                    fn()
+        return g
+
+    step_graph = capture(step.step)
+    op_graphs = [capture(lambda op=op: step.launch(op)) for op in step.ops]
+    replays = max(1, args.steps // GRAPH_REPEAT)
+    for g in [step_graph] + op_graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        start.record()
+        for _ in range(replays):
+            step_graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    total_ms = start.elapsed_time(end) * args.steps / (replays * GRAPH_REPEAT)
+    op_ms = []
+    for g in op_graphs:
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(replays):
+            g.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        op_ms.append(s0.elapsed_time(s1) / (replays * GRAPH_REPEAT))
+    del step_graph, op_graphs
+    return total_ms, op_ms, sampler
+
+
 # ---------------------------------------------------------------- CPU legs
 
 class CpuLayerSample:
@@ -474,24 +533,28 @@ def gpu_arm(args, cfg):
     step = LayerStep(cfg, dev, tokens, pos_offset, ops)
     nops = len(step.ops)
     op_bytes = step.bytes()
+    use_graph = args.graph == "on" or (args.graph == "auto" and tokens <= 2048)
     for _ in range(args.warmup):
         step.step()
     torch.cuda.synchronize()
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
-              for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    with sampler:
-        for i in range(args.steps):
-            step.step(events[i])
-        torch.cuda.synchronize()
+    if use_graph:
+        total_ms, op_ms, sampler = graph_timing(step, args, world)
+    else:
+        events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
+                  for _ in range(args.steps)]
         if world > 1:
             dist.barrier()
-    total_ms = events[0][0].elapsed_time(events[-1][nops])
-    op_ms = [sum(events[i][j].elapsed_time(events[i][j + 1])
-                 for i in range(args.steps)) / args.steps for j in range(nops)]
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local)
+        with sampler:
+            for i in range(args.steps):
+                step.step(events[i])
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+        total_ms = events[0][0].elapsed_time(events[-1][nops])
+        op_ms = [sum(events[i][j].elapsed_time(events[i][j + 1])
+                     for i in range(args.steps)) / args.steps for j in range(nops)]
     bits = torch.zeros(1, dtype=torch.int32)
     bits.copy_(step.d["status"])
     if int(bits.item()) != 0:
@@ -553,6 +616,7 @@ def gpu_arm(args, cfg):
             "value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
+        "timing": "cuda graph replay" if use_graph else "direct launches",
         "gpu_launches": args.steps * sum(
             step.cfg.n_heads if o == "softmax" else 1 for o in step.ops),
     }
@@ -581,6 +645,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ops", default="",
                     help="comma list: time only these operators of the step")
+    ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
+                    help="replay the step from a CUDA graph (auto: T <= 2048)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="token rows per step instead of the workload's T")
     args = ap.parse_args()
