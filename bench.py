@@ -628,6 +628,138 @@ def gpu_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- sweep
+
+SWEEP_OPS = ("rmsnorm", "res_rmsnorm", "swiglu", "emb_q8_0", "emb_q4_0", "emb_q4_1")
+
+
+def sweep(args):
+    """Bandwidth sweep: every operator x hidden size x token
+    count, seed 1, quant tables of 32000 rows; one JSON line per point with
+    GB/s per GPU and the fractions of the measured and spec peaks.  Weak
+    scaling under torchrun: every rank runs the point on its own GPU and the
+    slowest rank's time is reported."""
+    import torch
+    import torch.distributed as dist
+    import mlb
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    peak, peak_kind = measured_peak()
+    ops = args.sweep_ops.split(",") if args.sweep_ops else SWEEP_OPS
+    hiddens = [int(h) for h in args.sweep_hidden.split(",")] if args.sweep_hidden \
+        else wl.SWEEP_HIDDEN
+    tokens_list = [int(t) for t in args.sweep_tokens.split(",")] if args.sweep_tokens \
+        else wl.SWEEP_TOKENS
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    f32 = dict(device=dev, dtype=torch.float32)
+    for op in ops:
+        for H in hiddens:
+            table = None
+            if op.startswith("emb"):
+                qt = {"emb_q8_0": wl.Q8_0, "emb_q4_0": wl.Q4_0,
+                      "emb_q4_1": wl.Q4_1}[op]
+                table = wl.quant_table(qt, wl.SWEEP_VOCAB, H, dev, seed=1)
+            for T in tokens_list:
+                if op in ("rmsnorm", "res_rmsnorm"):
+                    x = torch.randn((T, H), generator=g, **f32)
+                    r = torch.randn((T, H), generator=g, **f32) \
+                        if op == "res_rmsnorm" else None
+                    w = torch.randn((H,), generator=g, **f32) * 0.1 + 1
+                    h = torch.empty_like(x) if r is not None else None
+                    y = torch.empty_like(x)
+                    fn = lambda: mlb.rms_norm(x, w, 1e-5, residual=r, h_out=h, out=y)  # noqa: E731
+                    nbytes = (16 if r is not None else 8) * T * H + 4 * H
+                elif op == "swiglu":
+                    a = torch.randn((T, H), generator=g, **f32)
+                    b = torch.randn((T, H), generator=g, **f32)
+                    o = torch.empty_like(a)
+                    fn = lambda: mlb.swiglu(a, b, out=o)  # noqa: E731
+                    nbytes = 12 * T * H
+                else:
+                    tok = torch.randint(0, wl.SWEEP_VOCAB, (T,), generator=g,
+                                        device=dev, dtype=torch.int32)
+                    o = torch.empty((T, H), **f32)
+                    fn = lambda: mlb.embedding_rows(table, qt, wl.SWEEP_VOCAB, H, tok,  # noqa: E731
+                                                    out=o)
+                    nbytes = T * (wl.row_bytes(qt, H) + 4 * H + 4)
+                ms = time_fn(fn, nbytes, world)
+                if rank == 0:
+                    gbs = nbytes / (ms / 1e3) / 1e9
+                    print(json.dumps({
+                        "sweep": op, "hidden": H, "tokens_per_gpu": T,
+                        "n_gpus": world, "ms": round(ms, 5),
+                        "tokens_per_s": round(T * world / (ms / 1e3), 1),
+                        "gbs_per_gpu": round(gbs, 1),
+                        "frac_of_measured": round(gbs / peak, 4),
+                        "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
+                        "peak_kind": peak_kind}), flush=True)
+                del fn
+                torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+L2_BYTES = 126 * 1024 * 1024
+_flush_buf = None
+
+
+def time_fn(fn, nbytes, world):
+    """Device time of one launch.  Working sets under 2 x L2 are timed cold:
+    each launch sits alone between two events with a 512 MiB buffer written
+    before it (flushing L2; the fill also covers the host's enqueue time, so
+    the events bracket only the kernel), and the median of 21 launches is
+    kept.  Larger
+    ones are timed back to back (inputs larger than L2) over enough launches
+    for ~20 ms of device time."""
+    import torch
+    import torch.distributed as dist
+    global _flush_buf
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if nbytes < 2 * L2_BYTES:
+        if _flush_buf is None:
+            _flush_buf = torch.empty(512 * 1024 * 1024 // 4, device="cuda")
+        times = []
+        for _ in range(21):
+            _flush_buf.fill_(1.0)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+    else:
+        reps = int(min(2000, max(5, 20.0 / (nbytes / 6.5e9))))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -649,8 +781,16 @@ def main():
                     help="replay the step from a CUDA graph (auto: T <= 2048)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="token rows per step instead of the workload's T")
+    ap.add_argument("--sweep", action="store_true",
+                    help="bandwidth sweep: one JSON line per (op, H, T) point")
+    ap.add_argument("--sweep-ops", default="")
+    ap.add_argument("--sweep-hidden", default="")
+    ap.add_argument("--sweep-tokens", default="")
     args = ap.parse_args()
     cfg = wl.CONFIGS[args.workload]
+    if args.sweep:
+        sweep(args)
+        return
     if args.impl == "reference":
         reference_arm(args, cfg)
     else:
