@@ -12,15 +12,23 @@
 // Layout: x, r, h, y are [rows, cols] fp32 row-major; w is [cols].
 // Kernels:
 //   RmsNormWarpKernel  — cols <= 1024: one warp per row, row in registers,
-//                        shuffle-only reduction, 8 rows per 256-thread CTA.
+//                        shuffle-only reduction, up to 8 rows per CTA.
 //   RmsNormBlockKernel — cols <= 32768: one CTA per row, NV float4 per
 //                        thread held in registers, warp shuffle + one smem
 //                        exchange per row.
+//   RmsNormClusterKernel — few rows (a decode batch, rows < 2 x SMs) with
+//                        cols > 1024: a thread-block cluster of S <= 8 CTAs
+//                        shares each row; every CTA reduces its column slice
+//                        and reads the other CTAs' partial sums of squares
+//                        through distributed shared memory, so S times more
+//                        SMs work on the batch.
 //   RmsNormScalarKernel— any other shape/alignment: two passes, the second
 //                        re-reading the row (from L2 for realistic sizes).
 // HBM roofline: 16*rows*cols + 4*cols bytes with a residual (read x, r;
 // write h, y), 8*rows*cols + 4*cols without.
 #include <climits>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -150,6 +158,64 @@ __global__ void __launch_bounds__(1024) RmsNormBlockKernel(RmsArgs a) {
   }
 }
 
+// One row per cluster (blockIdx.x = row), S = cluster size CTAs along y.
+// CTA rank r owns float4 columns [r*chunk, min((r+1)*chunk, c4)), NV per
+// thread.  The partial sums are combined in rank order (deterministic).
+template <int NV, bool RES>
+__global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float scratch[32];
+  __shared__ float partial;
+  const int c4 = a.cols >> 2;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int ranks = static_cast<int>(cluster.num_blocks());
+  const int c_begin = rank * chunk;
+  const int c_end = min(c4, c_begin + chunk);
+  const int64_t row = blockIdx.x;
+  const size_t off = static_cast<size_t>(row) * c4;
+  const float4* x4 = reinterpret_cast<const float4*>(a.x) + off;
+  float4 v[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = c_begin + threadIdx.x + blockDim.x * k;
+    v[k] = i < c_end ? LoadStream(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (RES) {
+    const float4* r4 = reinterpret_cast<const float4*>(a.res) + off;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = c_begin + threadIdx.x + blockDim.x * k;
+      if (i < c_end) v[k] = AddRn(v[k], LoadStream(r4 + i));
+    }
+    if (a.h != nullptr) {
+      float4* h4 = reinterpret_cast<float4*>(a.h) + off;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int i = c_begin + threadIdx.x + blockDim.x * k;
+        if (i < c_end) StoreStream(h4 + i, v[k]);
+      }
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) ss = SumSq(v[k], ss);
+  ss = BlockSum(ss, scratch);
+  if (threadIdx.x == 0) partial = ss;
+  cluster.sync();  // every CTA's partial is visible cluster-wide
+  float total = 0.0f;
+  for (int r = 0; r < ranks; ++r) total += *cluster.map_shared_rank(&partial, r);
+  cluster.sync();  // no CTA leaves while others still read its partial
+  const float inv = InvRms(total, a.n_f, a.eps);
+  const float4* w4 = reinterpret_cast<const float4*>(a.w);
+  float4* y4 = reinterpret_cast<float4*>(a.y) + off;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = c_begin + threadIdx.x + blockDim.x * k;
+    if (i < c_end) StoreStream(y4 + i, Scale(v[k], inv, __ldg(w4 + i)));
+  }
+}
+
 template <bool RES>
 __global__ void __launch_bounds__(256) RmsNormScalarKernel(RmsArgs a) {
   __shared__ float scratch[2][32];
@@ -186,10 +252,22 @@ __global__ void __launch_bounds__(256) RmsNormScalarKernel(RmsArgs a) {
 
 constexpr int64_t kMaxGrid = 1 << 24;
 
+// Warps per CTA for the warp-per-row kernels: 8 when there are rows enough
+// to fill every SM twice over, fewer for small batches so that the rows
+// spread over more SMs (256 rows at cols 896 -> 256 one-warp CTAs).
+int WarpsPerCta(int64_t rows) {
+  const int64_t fill = 2 * static_cast<int64_t>(SmCount());
+  int64_t w = rows / fill;
+  if (w < 1) w = 1;
+  if (w > 8) w = 8;
+  return static_cast<int>(w);
+}
+
 template <bool RES>
 int LaunchWarp(const RmsArgs& a, int nv, cudaStream_t s) {
-  const int threads = 256;
-  const int64_t blocks = (a.rows + 7) / 8;
+  const int wpc = WarpsPerCta(a.rows);
+  const int threads = 32 * wpc;
+  const int64_t blocks = (a.rows + wpc - 1) / wpc;
   const dim3 grid(static_cast<unsigned>(blocks < kMaxGrid ? blocks : kMaxGrid));
   switch (nv) {
 #define MLB_CASE(N) \
@@ -212,6 +290,42 @@ int LaunchBlock(const RmsArgs& a, int nv, int threads, cudaStream_t s) {
     MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
     default: return Fail(MLB_ERR_ARG, "rmsnorm: bad block width");
+  }
+  return CheckLaunch("mlb_rmsnorm_f32");
+}
+
+// Few long rows: a cluster of `ranks` CTAs per row (rows <= 65535 so the
+// row index fits blockIdx.x of a y-clustered grid).
+template <bool RES>
+int LaunchCluster(const RmsArgs& a, int ranks, cudaStream_t s) {
+  const int c4 = a.cols / 4;
+  const int chunk = (c4 + ranks - 1) / ranks;
+  int nv = (chunk + 255) / 256;
+  int threads = (chunk + nv - 1) / nv;
+  threads = (threads + 31) / 32 * 32;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(a.rows), static_cast<unsigned>(ranks), 1);
+  config.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  config.dynamicSmemBytes = 0;
+  config.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(ranks);
+  attr[0].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  cudaError_t err = cudaErrorInvalidValue;
+  switch (nv) {
+    case 1: err = cudaLaunchKernelEx(&config, RmsNormClusterKernel<1, RES>, a, chunk); break;
+    case 2: err = cudaLaunchKernelEx(&config, RmsNormClusterKernel<2, RES>, a, chunk); break;
+    case 3: err = cudaLaunchKernelEx(&config, RmsNormClusterKernel<3, RES>, a, chunk); break;
+    case 4: err = cudaLaunchKernelEx(&config, RmsNormClusterKernel<4, RES>, a, chunk); break;
+    default: return Fail(MLB_ERR_ARG, "rmsnorm: bad cluster width");
+  }
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return Fail(MLB_ERR_CUDA, std::string("mlb_rmsnorm_f32: ") + cudaGetErrorString(err));
   }
   return CheckLaunch("mlb_rmsnorm_f32");
 }
@@ -247,6 +361,17 @@ extern "C" int mlb_rmsnorm_f32(const float* x, const float* residual,
   if (vec && cols <= 1024) {
     const int nv = static_cast<int>((c4 + 31) / 32);
     return res ? LaunchWarp<true>(a, nv, s) : LaunchWarp<false>(a, nv, s);
+  }
+  // few long rows: spread each row over a cluster of up to 8 CTAs
+  const int64_t fill = 2 * static_cast<int64_t>(SmCount());
+  if (vec && cols > 1024 && cols <= 32768 && rows < fill) {
+    int64_t ranks = (fill + rows - 1) / rows;
+    if (ranks > 8) ranks = 8;  // portable cluster size
+    // each CTA holds at most 1024 float4s of its row (4 per thread x 256)
+    if (ranks > 1 && (c4 + ranks - 1) / ranks <= 1024) {
+      const int r = static_cast<int>(ranks);
+      return res ? LaunchCluster<true>(a, r, s) : LaunchCluster<false>(a, r, s);
+    }
   }
   if (vec && cols <= 32768) {
     int nv = static_cast<int>((c4 + 255) / 256);

@@ -56,7 +56,13 @@ __device__ __forceinline__ void Rotate(float& x0, float& x1, float c, float s) {
 // every CTA streams one contiguous q row and one k row.  (Measured on B200
 // at 40 heads x 128: 6.27 TB/s, against 5.83 TB/s for one item per thread
 // over a flat grid and 5.73 TB/s for a 2-D token x chunk grid.)
-template <bool NEOX>
+// With few tokens (a decode batch) a token's items are split over
+// gridDim.y CTAs so that every SM gets work: CTA (x, y) walks items
+// y*blockDim.x, stepping by gridDim.y*blockDim.x.
+// SPLIT is a template flag so that the unsplit form (large batches) keeps
+// full occupancy: its item loop is a chain of dependent load -> store steps,
+// and the extra index registers of the split form cost 2 of 8 CTAs per SM.
+template <bool NEOX, bool SPLIT>
 __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
   const int half = a.hd >> 1;
   const int groups = NEOX ? (a.hd >> 3) : (a.hd >> 2);  // per head
@@ -65,11 +71,13 @@ __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
     const int64_t pos =
         a.positions != nullptr ? __ldg(a.positions + t) : a.position_base + t;
     const bool ok = pos >= 0 && pos < a.table_rows;
-    if (!ok && threadIdx.x == 0 && a.status != nullptr)
+    if (!ok && threadIdx.x == 0 && (!SPLIT || blockIdx.y == 0) &&
+        a.status != nullptr)
       atomicOr(a.status, MLB_STATUS_BAD_POSITION);
     const float4* trow = reinterpret_cast<const float4*>(
         a.table + static_cast<size_t>(ok ? pos : 0) * a.hd);
-    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    for (int it = SPLIT ? blockIdx.y * blockDim.x + threadIdx.x : threadIdx.x;
+         it < items; it += SPLIT ? gridDim.y * blockDim.x : blockDim.x) {
       const int head = it / groups;
       const int g = it - head * groups;
       const bool is_q = head < a.nq;
@@ -182,10 +190,18 @@ extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
   if (threads < 32) threads = 32;
   cudaStream_t s = AsStream(stream);
   if (vec) {
-    if (neox) {
-      RopeVecKernel<true><<<grid, threads, 0, s>>>(a);
+    // split tokens over several CTAs when they cannot fill every SM twice
+    const int64_t fill = 2 * static_cast<int64_t>(SmCount());
+    int64_t split = rows < fill ? (fill + rows - 1) / rows : 1;
+    const int64_t max_split = (items + threads - 1) / threads;
+    if (split > max_split) split = max_split;
+    const dim3 grid2(grid.x, static_cast<unsigned>(split));
+    if (split > 1) {
+      if (neox) RopeVecKernel<true, true><<<grid2, threads, 0, s>>>(a);
+      else RopeVecKernel<false, true><<<grid2, threads, 0, s>>>(a);
     } else {
-      RopeVecKernel<false><<<grid, threads, 0, s>>>(a);
+      if (neox) RopeVecKernel<true, false><<<grid, threads, 0, s>>>(a);
+      else RopeVecKernel<false, false><<<grid, threads, 0, s>>>(a);
     }
   } else {
     RopeScalarKernel<<<grid, 256, 0, s>>>(a, neox);

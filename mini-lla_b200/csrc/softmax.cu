@@ -208,11 +208,16 @@ extern "C" int mlb_softmax_rows_f32(const float* x, float* y, int64_t rows,
   const int64_t c4 = cols / 4;
   if (vec && cols <= 1024) {
     const int nv = static_cast<int>((c4 + 31) / 32);
-    const int64_t blocks = (rows + 7) / 8;
+    // up to 8 rows (warps) per CTA; fewer when rows are too few to fill
+    // every SM twice
+    int64_t wpc = rows / (2 * static_cast<int64_t>(SmCount()));
+    wpc = wpc < 1 ? 1 : (wpc > 8 ? 8 : wpc);
+    const int64_t blocks = (rows + wpc - 1) / wpc;
+    const int threads = static_cast<int>(32 * wpc);
     const dim3 grid(static_cast<unsigned>(blocks < kMaxGrid ? blocks : kMaxGrid));
     switch (nv) {
 #define MLB_CASE(N) \
-  case N: SoftmaxWarpKernel<N><<<grid, 256, 0, s>>>(a); break;
+  case N: SoftmaxWarpKernel<N><<<grid, threads, 0, s>>>(a); break;
       MLB_CASE(1) MLB_CASE(2) MLB_CASE(3) MLB_CASE(4)
       MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
