@@ -29,6 +29,12 @@
 namespace mlb {
 namespace {
 
+// Rows up to this many bytes are staged one per warp when there are rows
+// enough to fill every SM (B200 sweep: Q8_0 at cols 2048 1.08 vs 0.79 of the
+// copy peak, Q4_1 at cols 4096 1.03 vs 0.88; Q8_0 at cols 4096 — 4352-byte
+// rows — is faster one row per CTA).
+constexpr int64_t kWarpRowBytes = 2560;
+
 // Largest staged row (bytes of dynamic shared memory without an opt-in):
 // Q8_0 rows up to cols ~ 45000.  Longer rows take the scalar kernel.
 constexpr int64_t kMaxStagedBytes = 48 * 1024;
@@ -165,10 +171,10 @@ __global__ void __launch_bounds__(256) EmbeddingStagedKernel(EmbArgs a,
   }
 }
 
-// Short rows (cols <= 1024, at most 32 blocks): one warp per token row, up to
-// 8 rows per CTA, each warp staging its own row in its slice of shared
-// memory (`slice` bytes) — a CTA per ~300-byte row would be mostly launch
-// and barrier overhead.
+// Short rows (cols <= 1024, or rows of at most kWarpRowBytes in a large
+// batch): one warp per token row, up to 8 rows per CTA, each warp staging its
+// own row in its slice of shared memory (`slice` bytes) — a CTA per short
+// row would be mostly launch and barrier overhead.
 template <int QT>
 __global__ void __launch_bounds__(256) EmbeddingStagedWarpKernel(EmbArgs a,
                                                                  int64_t table_bytes,
@@ -301,7 +307,8 @@ int LaunchEmbedding(const void* table, int qtype, int64_t vocab, int64_t cols,
   const int64_t table_bytes_all = vocab * row_bytes;
   if (vec && qtype == MLB_F32 && (tbl & 15u) == 0) {
     EmbeddingF32Kernel<<<grid, threads, 0, s>>>(a);
-  } else if (vec && qtype != MLB_F32 && cols <= 1024) {
+  } else if (vec && qtype != MLB_F32 &&
+             (cols <= 1024 || (rows >= fill && row_bytes <= kWarpRowBytes))) {
     // warp per row; 8 rows per CTA unless rows are too few to fill the SMs
     int64_t wpc = rows / fill;
     wpc = wpc < 1 ? 1 : (wpc > 8 ? 8 : wpc);
