@@ -631,6 +631,45 @@ def gpu_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- linear
+
+LINEAR_SHAPES = ((14336, 4096), (4096, 14336), (4864, 896), (896, 4864))
+
+
+def linear_bench(args):
+    """Decode-path linear layer (mlb_linear_f32): one JSON line per
+    (format, n, k, tokens) — LLaMA-3-8B FFN gate/up [14336, 4096] and down
+    [4096, 14336], Qwen2-0.5B FFN [4864, 896] / [896, 4864] — with GB/s over
+    the weight bytes + activations, timed cold (L2 flushed) when the weights
+    fit in L2."""
+    import torch
+    import mlb
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = measured_peak()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    for qt in (wl.Q8_0, wl.Q4_0, wl.Q4_1, wl.F32):
+        for n, k in LINEAR_SHAPES:
+            w = wl.quant_table(qt, n, k, dev, seed=1)
+            for t in (1, 4, 8):
+                x = torch.randn((t, k), generator=g, device=dev)
+                y = torch.empty((t, n), device=dev)
+                fn = lambda: mlb.linear(w, qt, n, k, x, out=y)  # noqa: E731
+                nbytes = n * wl.row_bytes(qt, k) + 4 * t * (k + n)
+                ms = time_fn(fn, nbytes, 1)
+                gbs = nbytes / (ms / 1e3) / 1e9
+                print(json.dumps({
+                    "linear": wl.QNAME[qt], "n": n, "k": k, "tokens": t,
+                    "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                    "frac_of_measured": round(gbs / peak, 4),
+                    "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
+                    "peak_kind": peak_kind,
+                    "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}),
+                    flush=True)
+            del w
+            torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------- sweep
 
 SWEEP_OPS = ("rmsnorm", "res_rmsnorm", "swiglu", "emb_q8_0", "emb_q4_0", "emb_q4_1")
@@ -786,6 +825,8 @@ def main():
                     help="token rows per step instead of the workload's T")
     ap.add_argument("--sweep", action="store_true",
                     help="bandwidth sweep: one JSON line per (op, H, T) point")
+    ap.add_argument("--linear", action="store_true",
+                    help="decode-path linear layer: one JSON line per shape")
     ap.add_argument("--sweep-ops", default="")
     ap.add_argument("--sweep-hidden", default="")
     ap.add_argument("--sweep-tokens", default="")
@@ -793,6 +834,9 @@ def main():
     cfg = wl.CONFIGS[args.workload]
     if args.sweep:
         sweep(args)
+        return
+    if args.linear:
+        linear_bench(args)
         return
     if args.impl == "reference":
         reference_arm(args, cfg)

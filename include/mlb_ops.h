@@ -189,6 +189,22 @@ int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
                       int64_t cols, int32_t token, float* out, void* stream);
 
 /*
+ * Linear layer for decode-sized batches: y[t] = W · x[t] for t < t_rows.
+ * Replaces CudaLinear (include/mini_llama/cuda_matmul.h:11, cuda_matmul.cu:
+ * 41-101 block GEMV kernels and the cuBLAS SGEMV F32 path :122-133; CPU
+ * quant.cc:171-226 LinearWithBlocks, matmul_optimized.cc:95-117).
+ *   w: n rows of mlb_row_bytes(qtype, k) bytes (ggml blocks or F32), the
+ *   reference's weight layout; x: [t_rows, k]; y: [t_rows, n].
+ * Every block's 32 products are summed before its scale is applied and the
+ * row is reduced across a warp, so y matches the reference's sequential sum
+ * within |y - y_ref| <= 1e-5 * sum_i |w_i x_i|.  Weights are read once per
+ * group of 8 tokens; k % 32 != 0 or unaligned x take a scalar path that keeps
+ * the reference's summation order.
+ */
+int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
+                   const float* x, int64_t t_rows, float* y, void* stream);
+
+/*
  * Helper for synchronous callers: waits for `stream`, copies the device
  * status word to the host, and returns MLB_OK when it is zero, MLB_ERR_RANGE
  * when a bit is set (the bits are stored in *bits_host when non-NULL), or

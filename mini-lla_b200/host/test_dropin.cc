@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "mini_llama/cuda_layer_ops.h"
+#include "mini_llama/cuda_matmul.h"
 #include "mini_llama/cuda_ops.h"
 #include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
@@ -324,6 +325,35 @@ void TestRuntime() {
   Expect(Throws([] { CudaSetDevice(1 << 20); }), "bad device index throws");
 }
 
+// CudaLinear (cuda_matmul.h) against the reference's quantised / F32 Linear.
+void TestLinear(std::mt19937& rng) {
+  for (QuantType type : {QuantType::kF32, QuantType::kQ8_0, QuantType::kQ4_0,
+                         QuantType::kQ4_1}) {
+    for (int cols : {4096, 896, 40}) {
+      const int rows = 300;
+      const Tensor values = Random({rows, cols}, rng);
+      const QuantizedTensor w = Quantize(values, type);
+      const CudaWeight dw = TableWeight(w);
+      const Tensor x = Random({cols}, rng);
+      const Tensor want = Linear(x, w);
+      const Tensor got = CudaLinear(CudaTensor::FromHost(x), dw).Download();
+      // |got - want| <= 1e-5 * sum_i |w_i x_i|
+      std::vector<float> row(cols);
+      bool ok = got.Size() == want.Size();
+      for (int j = 0; ok && j < rows; ++j) {
+        DequantizeRow(w, j, row.data());
+        double mag = 0;
+        for (int i = 0; i < cols; ++i) mag += std::fabs(double(row[i]) * x.data[i]);
+        ok = std::fabs(double(got.data[j]) - want.data[j]) <= 1e-5 * mag + 1e-30;
+      }
+      Expect(ok, std::string("CudaLinear ") + QuantTypeName(type) +
+                     " cols=" + std::to_string(cols));
+    }
+  }
+  const CudaWeight dw = TableWeight(Quantize(Random({4, 64}, rng), QuantType::kQ8_0));
+  Expect(Throws([&] { CudaLinear(CudaTensor({63}), dw); }), "CudaLinear size mismatch throws");
+}
+
 // One host thread per "device" entry; a single-GPU box lists device 0 twice
 // (independent token ranges, no waits between them).
 void TestShardingAndWaits(std::mt19937& rng) {
@@ -403,6 +433,7 @@ int main() {
     TestEmbedding(rng);
     TestBatched(rng);
     TestShardingAndWaits(rng);
+    TestLinear(rng);
     TestRuntime();
   } catch (const std::exception& e) {
     std::printf("FAIL: unexpected exception: %s\n", e.what());

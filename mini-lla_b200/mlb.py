@@ -50,6 +50,8 @@ SIGNATURES = {
                                      c_void_p, c_int64, c_void_p, c_void_p,
                                      c_void_p]),
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "mlb_linear_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
+                               c_int64, c_void_p, c_void_p]),
 }
 
 _lib = None
@@ -295,6 +297,25 @@ def embedding_row(table, qtype: int, vocab: int, cols: int, token: int,
         out = torch.empty((cols,), dtype=torch.float32, device=table.device)
     _check(load().mlb_embedding_row(_ptr(table), qtype, vocab, cols, int(token),
                                     _ptr(out), _stream(stream)), "embedding_row")
+    return out
+
+
+def linear(weight, qtype: int, n: int, k: int, x, out=None, stream=None):
+    """y = x · dequant(W)^T for x [T, k] (or [k]) -> [T, n] (or [n])."""
+    import torch
+    op = "linear"
+    _require(weight.is_cuda and weight.is_contiguous(), op,
+             "weight must be a contiguous CUDA tensor")
+    _require(weight.numel() * weight.element_size() >= n * row_bytes(qtype, k), op,
+             "weight smaller than n rows")
+    _f32_cuda(x, op, "x")
+    _require(x.shape[-1] == k, op, "input size mismatch")
+    t_rows = x.numel() // k
+    if out is None:
+        shape = (n,) if x.dim() == 1 else (t_rows, n)
+        out = torch.empty(shape, dtype=torch.float32, device=x.device)
+    _check(load().mlb_linear_f32(_ptr(weight), qtype, n, k, _ptr(x), t_rows,
+                                 _ptr(out), _stream(stream)), op)
     return out
 
 

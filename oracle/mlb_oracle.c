@@ -287,3 +287,37 @@ int64_t mlbo_rope_rows(float* q, float* k, const float* bq, const float* bk,
   }
   return bad;
 }
+
+/* Linear layer y[t] = W · x[t] over a table of `n` rows x `k` columns (the
+ * weight layout of the embedding table: ggml blocks or F32 rows).
+ * Quantised: reference src/quant.cc:171-185 (DotQuantizedRow: sequential
+ * sum of DequantizeElement(w) * x, each product and partial sum rounded) and
+ * :202-226 (LinearWithBlocks, one dot per (row, output)).
+ * F32: src/matmul_optimized.cc:95-117 (LinearOptimized: sum += x[k] * w[k]).
+ * x is [t_rows, k], y is [t_rows, n]. */
+void mlbo_linear_rows(const void* table, int qtype, int64_t n, int64_t k,
+                      const float* x, int64_t t_rows, float* y) {
+  const uint8_t* base = (const uint8_t*)table;
+  const int64_t row_bytes = mlbo_row_bytes(qtype, k);
+  const int bb = mlbo_block_bytes(qtype);
+  for (int64_t t = 0; t < t_rows; ++t) {
+    const float* xt = x + t * k;
+    for (int64_t j = 0; j < n; ++j) {
+      const uint8_t* row = base + j * row_bytes;
+      float sum = 0.0f;
+      if (qtype == MLBO_F32) {
+        const float* w = (const float*)row;
+        for (int64_t i = 0; i < k; ++i) sum += xt[i] * w[i];
+      } else {
+        const int64_t blocks = (k + MLBO_BLOCK - 1) / MLBO_BLOCK;
+        for (int64_t b = 0; b < blocks; ++b) {
+          const int64_t begin = b * MLBO_BLOCK;
+          const int64_t end = begin + MLBO_BLOCK < k ? begin + MLBO_BLOCK : k;
+          for (int64_t i = begin; i < end; ++i)
+            sum += dequant_element(qtype, row + b * bb, (int)(i - begin)) * xt[i];
+        }
+      }
+      y[t * n + j] = sum;
+    }
+  }
+}

@@ -58,6 +58,8 @@ class Oracle:
             "mlbo_softmax_rows": (c_int64, [c_void_p, c_void_p, c_int64, c_int64,
                                             c_void_p]),
             "mlbo_rope_table": (None, [c_float, c_int, c_int64, c_int64, c_void_p]),
+            "mlbo_linear_rows": (None, [c_void_p, c_int, c_int64, c_int64, c_void_p,
+                                        c_int64, c_void_p]),
             "mlbo_rope_rows": (c_int64, [c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_int64, c_int, c_int, c_int,
                                          c_float, c_int]),
@@ -121,6 +123,15 @@ class Oracle:
         bad = self.lib.mlbo_softmax_rows(_p(x), _p(y), rows, cols, _p(vl))
         return y, bad
 
+    def linear(self, table, qtype, n, k, x):
+        """y = x · dequant(W)^T with the reference's sequential sums."""
+        x = _f32(x)
+        t_rows = x.size // k
+        y = np.empty((t_rows, n), dtype=np.float32)
+        self.lib.mlbo_linear_rows(_p(np.ascontiguousarray(table)), qtype, n, k,
+                                  _p(x), t_rows, _p(y))
+        return y
+
     def rope_table(self, theta, hd, pos_begin, pos_end):
         out = np.empty((pos_end - pos_begin, hd), dtype=np.float32)
         self.lib.mlbo_rope_table(theta, hd, pos_begin, pos_end, _p(out))
@@ -160,6 +171,7 @@ class Reference:
             "mlref_embedding_rows": (c_int, [V, c_int, c_int64, c_int64, V,
                                              c_int64, V]),
             "mlref_quantize": (c_int, [V, c_int64, c_int64, c_int, V]),
+            "mlref_linear": (c_int, [V, c_int, c_int64, c_int64, V, c_int64, V]),
             "mlref_rows_new": (V, [V, c_int64, c_int64]),
             "mlref_heads_new": (V, [V, c_int64, c_int, c_int]),
             "mlref_rows_free": (None, [V]),
@@ -232,6 +244,15 @@ class Reference:
         rc = self.lib.mlref_embedding_rows(_p(table), qtype, vocab, cols,
                                            _p(tokens), tokens.size, _p(out))
         return out, rc
+
+    def linear(self, table, qtype, n, k, x):
+        x = _f32(x)
+        t_rows = x.size // k
+        y = np.empty((t_rows, n), dtype=np.float32)
+        rc = self.lib.mlref_linear(_p(np.ascontiguousarray(table)), qtype, n, k,
+                                   _p(x), t_rows, _p(y))
+        assert rc == 0, rc
+        return y
 
     def quantize(self, values, qtype, row_bytes):
         values = _f32(values)

@@ -186,6 +186,19 @@ int mlref_embedding_rows(const void* table, int qtype, int64_t vocab,
   });
 }
 
+// Linear layer through the reference (quant.cc:306-318 -> LinearWithBlocks,
+// or the F32 LinearDispatch): x [t_rows, k] -> y [t_rows, n].
+int mlref_linear(const void* table, int qtype, int64_t n, int64_t k,
+                 const float* x, int64_t t_rows, float* y) {
+  return Guard([&] {
+    const QuantizedTensor w = MakeTable(table, qtype, n, k);
+    Tensor input({static_cast<int>(t_rows), static_cast<int>(k)});
+    std::memcpy(input.data.data(), x, 4 * t_rows * k);
+    const Tensor out = mini_lla::Linear(input, w);
+    std::memcpy(y, out.data.data(), 4 * t_rows * n);
+  });
+}
+
 // Quantize through the reference's own quantisers (quant.cc:230-266); used
 // only to build realistic fixtures.  out must hold the table's block bytes.
 int mlref_quantize(const float* values, int64_t rows, int64_t cols, int qtype,

@@ -1,0 +1,87 @@
+"""Linear layer (mlb_linear_f32) vs the reference's LinearWithBlocks / F32
+Linear (quant.cc:171-226, matmul_optimized.cc:95-117) through the C ABI.
+
+The vector path sums each block's 32 products before scaling and reduces a
+row across a warp, so it is checked within |y - y_ref| <= 1e-5 * sum|w x|
+(the magnitude of the dot product's terms); the scalar path (k % 32 != 0)
+keeps the reference's sequential order and must match bit for bit.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_bitexact
+
+import mlb
+import workloads as wl
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, device):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _check(got, want, wdeq, x, what):
+    mag = np.abs(x.astype(np.float64)) @ np.abs(wdeq.astype(np.float64)).T
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    bad = err > 1e-5 * mag + 1e-30
+    assert not bad.any(), (f"{what}: {bad.sum()} outputs off; worst ratio "
+                           f"{float((err / np.maximum(mag, 1e-30)).max()):.2e}")
+
+
+@pytest.mark.parametrize("qtype", [wl.F32, wl.Q8_0, wl.Q4_0, wl.Q4_1])
+@pytest.mark.parametrize("n,k,t", [(37, 96, 1), (300, 4096, 1), (64, 4096, 3),
+                                   (129, 1024, 8), (40, 2048, 9), (17, 3584, 17),
+                                   (2000, 896, 2)])
+def test_linear_vs_oracle(cuda, oracle, qtype, n, k, t):
+    import torch
+    rng = np.random.default_rng(n * 7 + k + t)
+    table = wl.numpy_quant_table(qtype, n, k, seed=n + k)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"{wl.QNAME[qtype]} n={n} k={k} t={t}")
+
+
+@pytest.mark.parametrize("qtype", [wl.F32, wl.Q8_0, wl.Q4_0, wl.Q4_1])
+def test_linear_scalar_path_bitexact(cuda, oracle, qtype):
+    """k not a multiple of 32 (tail block): the reference's order, bit-exact."""
+    import torch
+    rng = np.random.default_rng(qtype)
+    for n, k, t in ((33, 40, 2), (7, 38, 1), (12, 1000, 3)):
+        table = wl.numpy_quant_table(qtype, n, k, seed=k)
+        x = rng.standard_normal((t, k), dtype=np.float32)
+        got = mlb.linear(dev(table, cuda), qtype, n, k, dev(x, cuda))
+        torch.cuda.synchronize()
+        assert_bitexact(got.cpu().numpy(), oracle.linear(table, qtype, n, k, x),
+                        f"{wl.QNAME[qtype]} k={k}")
+
+
+def test_linear_llama3_ffn_shapes(cuda, oracle):
+    """Decode step of the LLaMA-3-8B FFN (Q8_0 gate [14336, 4096] and down
+    [4096, 14336]); sampled output rows against the oracle."""
+    import torch
+    rng = np.random.default_rng(1)
+    for n, k in ((14336, 4096), (4096, 14336)):
+        table_d = wl.quant_table(wl.Q8_0, n, k, cuda, seed=2)
+        x = rng.standard_normal((1, k), dtype=np.float32)
+        got = mlb.linear(table_d, wl.Q8_0, n, k, dev(x, cuda)).cpu().numpy()
+        rows = np.unique(np.r_[0, n - 1, rng.integers(0, n, 200)])
+        rb = wl.row_bytes(wl.Q8_0, k)
+        tbl = table_d.view(n, rb)[torch.from_numpy(rows).to(cuda)].cpu().numpy()
+        want = oracle.linear(tbl.reshape(-1), wl.Q8_0, rows.size, k, x)
+        wdeq, _ = oracle.embedding(tbl.reshape(-1), wl.Q8_0, rows.size, k,
+                                   np.arange(rows.size, dtype=np.int32))
+        _check(got[:, rows], want, wdeq, x, f"ffn {n}x{k}")
+
+
+def test_linear_rejects_bad_input(cuda):
+    import torch
+    w = torch.zeros(64 * 34, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError):
+        mlb.linear(w, wl.Q8_0, 3, 1024, torch.zeros(1024, device=cuda))
+    with pytest.raises(ValueError):
+        mlb.linear(w, wl.Q8_0, 1, 64, torch.zeros(63, device=cuda))

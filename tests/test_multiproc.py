@@ -67,10 +67,21 @@ def _worker(rank, world, port, mode, result_path):
         return
     out = _layer(Oracle(), b, lo, hi)
     if mode == "fail":
-        # rank 0 checks the failure flag between steps, before any collective
-        ok = store.check(["failed/1"])
+        # Between steps, before any collective, rank 0 waits (bounded) for
+        # rank 1's status on the store: a heartbeat or a failure record.
+        import time
+        deadline = time.monotonic() + 15.0
+        seen = "timeout"
+        while time.monotonic() < deadline:
+            if store.check(["failed/1"]):
+                seen = "saw-failure"
+                break
+            if store.check(["alive/1"]):
+                seen = "no-failure"
+                break
+            time.sleep(0.01)
         with open(result_path, "w") as f:
-            f.write("saw-failure" if ok else "no-failure")
+            f.write(seen)
         dist.destroy_process_group()
         return
     sizes = [None] * world
