@@ -217,3 +217,10 @@ def test_oracle_matches_reference_library(oracle, reference, seed):
         b, rc = reference.embedding(table, qtype, vocab, cols, tokens)
         assert bad == 0 and rc == 0
         assert_bitexact(a, b, wl.QNAME[qtype])
+        # linear layer over the same table (quant.cc:171-226 / F32 Linear)
+        for k in (cols, 40):
+            tab = wl.numpy_quant_table(qtype, 31, k, seed)
+            x = rng.standard_normal((3, k), dtype=np.float32)
+            assert_bitexact(oracle.linear(tab, qtype, 31, k, x),
+                            reference.linear(tab, qtype, 31, k, x),
+                            f"linear {wl.QNAME[qtype]} k={k}")
