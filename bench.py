@@ -648,10 +648,16 @@ def linear_bench(args):
     peak, peak_kind = measured_peak()
     g = torch.Generator(device=dev)
     g.manual_seed(1)
-    for qt in (wl.Q8_0, wl.Q4_0, wl.Q4_1, wl.F32):
-        for n, k in LINEAR_SHAPES:
+    qts = [wl.QTYPE_BY_NAME[q] for q in args.linear_qtypes.split(",")] \
+        if args.linear_qtypes else (wl.Q8_0, wl.Q4_0, wl.Q4_1, wl.F32)
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.linear_shapes.split(",")] \
+        if args.linear_shapes else LINEAR_SHAPES
+    tokens = [int(t) for t in args.linear_tokens.split(",")] \
+        if args.linear_tokens else (1, 4, 8)
+    for qt in qts:
+        for n, k in shapes:
             w = wl.quant_table(qt, n, k, dev, seed=1)
-            for t in (1, 4, 8):
+            for t in tokens:
                 x = torch.randn((t, k), generator=g, device=dev)
                 y = torch.empty((t, n), device=dev)
                 fn = lambda: mlb.linear(w, qt, n, k, x, out=y)  # noqa: E731
@@ -756,10 +762,10 @@ _flush_buf = None
 
 def time_fn(fn, nbytes, world):
     """Device time of one launch.  Working sets under 2 x L2 are timed cold:
-    each launch sits alone between two events with a 512 MiB buffer written
-    before it (flushing L2; the fill also covers the host's enqueue time, so
-    the events bracket only the kernel), and the median of 21 launches is
-    kept.  Larger
+    each launch sits alone between two events after a read of a 512 MiB
+    buffer (evicting L2 with clean lines) and a ~0.5 ms device sleep (during
+    which the host enqueues the launch, so the events bracket only the
+    kernel), and the median of 21 launches is kept.  Larger
     ones are timed back to back (inputs larger than L2) over enough launches
     for ~20 ms of device time."""
     import torch
@@ -773,10 +779,14 @@ def time_fn(fn, nbytes, world):
     torch.cuda.synchronize()
     if nbytes < 2 * L2_BYTES:
         if _flush_buf is None:
-            _flush_buf = torch.empty(512 * 1024 * 1024 // 4, device="cuda")
+            _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
         times = []
         for _ in range(21):
-            _flush_buf.fill_(1.0)
+            # a read-only pass evicts the inputs and leaves only clean lines
+            # (a write would leave dirty lines whose write-back would land in
+            # the timed kernel)
+            _flush_buf.sum()
+            torch.cuda._sleep(1_000_000)  # the host enqueues the launch meanwhile
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
@@ -827,6 +837,9 @@ def main():
                     help="bandwidth sweep: one JSON line per (op, H, T) point")
     ap.add_argument("--linear", action="store_true",
                     help="decode-path linear layer: one JSON line per shape")
+    ap.add_argument("--linear-qtypes", default="", help="e.g. Q8_0,F32")
+    ap.add_argument("--linear-shapes", default="", help="e.g. 14336x4096")
+    ap.add_argument("--linear-tokens", default="", help="e.g. 1,4")
     ap.add_argument("--sweep-ops", default="")
     ap.add_argument("--sweep-hidden", default="")
     ap.add_argument("--sweep-tokens", default="")

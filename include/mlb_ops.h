@@ -205,6 +205,43 @@ int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                    const float* x, int64_t t_rows, float* y, void* stream);
 
 /*
+ * KV-cache write: rows tokens' k and v ([rows, n_kv_heads * head_dim]) go to
+ * positions [position, position + rows) of one layer's cache, laid out as the
+ * reference's CudaKvCache layer [max_seq, n_kv_heads, head_dim]
+ * (cuda_attention.h:8-40; CudaKvCache::Write / KvWriteKernel
+ * cuda_attention.cu:13-23, 128-145; CPU kv_cache.cc:25-40).  Bit-exact copy.
+ * MLB_ERR_RANGE when the positions leave [0, max_seq).
+ */
+int mlb_kv_write_f32(float* keys, float* values, const float* k, const float* v,
+                     int64_t position, int64_t rows, int64_t max_seq,
+                     int n_kv_heads, int head_dim, void* stream);
+
+/* Floats of scratch mlb_attention_decode_f32 needs for these sizes and
+ * position (-1 for bad arguments). */
+int64_t mlb_attention_scratch_floats(int n_heads, int n_kv_heads, int head_dim,
+                                     int64_t position);
+
+/*
+ * Decode attention of one token at `position` over one layer's cache:
+ *   out[h] = softmax_t(q[h] . k_t / sqrt(head_dim)) . v_t,  t = 0..position,
+ * kv head h / (n_heads / n_kv_heads) for query head h (GQA, group <= 8).
+ * Replaces CudaAttention (cuda_attention.h:43-45, cuda_attention.cu:26-106,
+ * 147-195; CPU forward.cc:50-95).  q, out: [n_heads, head_dim]; keys, values:
+ * the layer's [max_seq, n_kv_heads, head_dim]; head_dim % 4 == 0, <= 256.
+ * The visible positions are split over CTAs (flash-decoding); each CTA reads
+ * a kv head's K/V rows once for all of its query heads and writes a partial
+ * softmax state to `scratch` (caller-owned device memory of at least
+ * mlb_attention_scratch_floats(...) floats), which a second kernel combines.
+ * Within 1e-5 * sum_t w_t |v_t| of the reference.  MLB_ERR_RANGE when
+ * position is outside [0, max_seq).
+ */
+int mlb_attention_decode_f32(const float* q, const float* keys,
+                             const float* values, float* out, int64_t position,
+                             int64_t max_seq, int n_heads, int n_kv_heads,
+                             int head_dim, float* scratch,
+                             int64_t scratch_floats, void* stream);
+
+/*
  * Helper for synchronous callers: waits for `stream`, copies the device
  * status word to the host, and returns MLB_OK when it is zero, MLB_ERR_RANGE
  * when a bit is set (the bits are stored in *bits_host when non-NULL), or

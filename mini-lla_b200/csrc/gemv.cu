@@ -3,19 +3,25 @@
 //
 // Reference arithmetic (src/quant.cc:171-185 DotQuantizedRow, :202-226
 // LinearWithBlocks; F32: src/matmul_optimized.cc:95-117): a sequential fp32
-// sum of dequant(w_i) * x_i per output.  Here each block's 32 products are
-// summed first and scaled once (d * Σ q_i x_i, plus m * Σ x_i for Q4_1), and
-// the block sums are reduced across a warp — the same value up to rounding:
+// sum of dequant(w_i) * x_i per output.  Here every 4 products of a block are
+// summed and scaled at once (d * Σ q_i x_i, plus m * Σ x_i for Q4_1), and the
+// partial sums are reduced across a warp — the same value up to rounding:
 // |y - y_ref| <= 1e-5 * Σ|w_i x_i| in the tests.  The reference GPU kernels
 // (cuda_matmul.cu:41-101) run one thread per output row over the whole row;
 // its F32 path calls cuBLAS SGEMV (:122-133).
 //
 // Design (memory-bound on W at T = 1):
-//   - one warp per output row, 8 rows per 256-thread CTA;
+//   - streaming form (x of all tokens fits in 96 KB of shared memory):
+//     persistent CTAs of 8 warps copy x once; each warp streams its rows in
+//     1024-column segments through a 4-deep cp.async ring (no CTA barrier on
+//     the weight stream);
+//   - chunked form otherwise: one warp per output row, 8 rows per CTA;
 //   - the CTA walks k in chunks of kChunk = 1024 columns (32 blocks): all
-//     threads stage x[:, chunk] for every token in shared memory (reused by
-//     the CTA's 8 rows), each warp stages its row's 32 blocks with 16-byte
-//     loads of the aligned window, and each lane decodes one block;
+//     threads copy x[:, chunk] for every token into shared memory (reused by
+//     the CTA's 8 rows), each warp copies its row's 32 blocks (the 16-byte
+//     aligned window) — both with cp.async, double-buffered so that chunk
+//     c + 1 is in flight while chunk c is computed — and lane l decodes the
+//     float4 groups l, l + 32, ... (8 lanes per block, conflict-free x reads);
 //   - block sums go to T fp32 accumulators per lane, reduced by shuffles.
 // HBM roofline per launch: n * row_bytes (weights) + 4 * T * (k + n).
 #include <climits>
@@ -41,23 +47,6 @@ struct GemvArgs {
 
 __device__ __forceinline__ uint32_t Smem16(const uint8_t* p) {
   return *reinterpret_cast<const unsigned short*>(p);
-}
-
-// 16-byte loads of table bytes [window, window + 16 * chunks) into dst; bytes
-// past the end of the table are not read.
-__device__ __forceinline__ void StageBytes(uint8_t* dst, const uint8_t* table,
-                                           int64_t window, int chunks,
-                                           int64_t table_bytes, int lane) {
-  for (int c = lane; c < chunks; c += 32) {
-    const int64_t off = window + 16 * static_cast<int64_t>(c);
-    if (off + 16 <= table_bytes) {
-      *reinterpret_cast<uint4*>(dst + 16 * c) =
-          __ldg(reinterpret_cast<const uint4*>(table + off));
-    } else {
-      for (int b = 0; b < 16; ++b)
-        dst[16 * c + b] = off + b < table_bytes ? table[off + b] : 0;
-    }
-  }
 }
 
 // Four quant values of one block (elements e..e+3), as floats.
@@ -91,86 +80,244 @@ __device__ __forceinline__ float Dot4(const float4& a, const float4& b, float ac
   return fmaf(a.w, b.w, acc);
 }
 
-// Dynamic shared memory: x chunk [T][kChunk] floats, then one weight-staging
-// slice of `slice` bytes per warp.
+// 16-byte global -> shared copies that bypass registers (cp.async), so a
+// lane keeps every copy of a chunk in flight at once.
+__device__ __forceinline__ void CopyAsync16(void* smem_dst, const void* gmem_src) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst),
+               "l"(gmem_src));
+}
+__device__ __forceinline__ void CopyAsyncCommit() {
+  asm volatile("cp.async.commit_group;\n" ::);
+}
+template <int N>
+__device__ __forceinline__ void CopyAsyncWait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Dynamic shared memory holds two stages; a stage is the x chunk
+// [T][kChunk] floats followed by one weight slice of `slice` bytes per warp.
+// Chunk c + 1 is copied in (cp.async) while chunk c is computed.
 template <int QT, int T>
 __global__ void __launch_bounds__(256) GemvKernel(GemvArgs a, int slice) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float4* xs = reinterpret_cast<float4*>(smem);
   constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  uint8_t* mine = smem + T * kChunk * 4 + warp * slice;
+  const int stage_bytes = T * kChunk * 4 + kWarpsPerCta * slice;
   const int64_t j = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + warp;
   const bool valid = j < a.n;
   const int k4 = a.k >> 2;
   const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  const int chunks = (a.k + kChunk - 1) / kChunk;
+
+  // Issues the copies of chunk `c` into stage `c & 1`; returns the byte
+  // offset of this warp's row start inside its weight slice.
+  auto stage_in = [&](int c) -> int {
+    uint8_t* st = smem + (c & 1) * stage_bytes;
+    const int c0 = c * kChunk;
+    const int c4 = min(kChunk, a.k - c0) >> 2;
+    float4* xs = reinterpret_cast<float4*>(st);
+    for (int i = threadIdx.x; i < T * c4; i += blockDim.x) {
+      const int t = i / c4;
+      const int q = i - t * c4;
+      CopyAsync16(xs + t * (kChunk / 4) + q,
+                  x4 + static_cast<int64_t>(t) * k4 + (c0 >> 2) + q);
+    }
+    if (QT == MLB_F32 || !valid) return 0;
+    uint8_t* mine = st + T * kChunk * 4 + warp * slice;
+    const int64_t start = j * a.row_bytes + static_cast<int64_t>(c0 / 32) * kBB;
+    const int64_t window = start & ~int64_t{15};
+    const int64_t end = start + static_cast<int64_t>((c4 * 4) / 32) * kBB;
+    const int n16 = static_cast<int>((end - window + 15) >> 4);
+    for (int q = lane; q < n16; q += 32) {
+      const int64_t off = window + 16 * static_cast<int64_t>(q);
+      if (off + 16 <= a.table_bytes) {
+        CopyAsync16(mine + 16 * q, a.w + off);
+      } else {
+        for (int b = 0; b < 16; ++b)
+          mine[16 * q + b] = off + b < a.table_bytes ? a.w[off + b] : 0;
+      }
+    }
+    return static_cast<int>(start - window);
+  };
+
   float acc[T];
 #pragma unroll
   for (int t = 0; t < T; ++t) acc[t] = 0.0f;
 
-  for (int c0 = 0; c0 < a.k; c0 += kChunk) {
-    const int cols = min(kChunk, a.k - c0);  // a multiple of 32
-    const int c4 = cols >> 2;
-    __syncthreads();  // the previous chunk is consumed
-    for (int i = threadIdx.x; i < T * c4; i += blockDim.x) {
-      const int t = i / c4;
-      const int c = i - t * c4;
-      xs[t * (kChunk / 4) + c] = __ldg(x4 + static_cast<int64_t>(t) * k4 + (c0 >> 2) + c);
-    }
-    int64_t start = 0, window = 0;
-    if (QT != MLB_F32 && valid) {
-      start = j * a.row_bytes + static_cast<int64_t>(c0 / 32) * kBB;
-      window = start & ~int64_t{15};
-      const int64_t end = start + static_cast<int64_t>(cols / 32) * kBB;
-      StageBytes(mine, a.w, window, static_cast<int>((end - window + 15) >> 4),
-                 a.table_bytes, lane);
-    }
-    __syncthreads();
-    if (!valid) continue;
-    if (QT == MLB_F32) {
-      const float4* wrow =
-          reinterpret_cast<const float4*>(a.w + j * a.row_bytes) + (c0 >> 2);
-      for (int c = lane; c < c4; c += 32) {
-        const float4 w = __ldg(wrow + c);
+  int lead = stage_in(0);
+  CopyAsyncCommit();
+  for (int c = 0; c < chunks; ++c) {
+    int next_lead = 0;
+    if (c + 1 < chunks) next_lead = stage_in(c + 1);
+    CopyAsyncCommit();   // (an empty group on the last chunk)
+    CopyAsyncWait<1>();  // chunk c has landed for this thread ...
+    __syncthreads();     // ... and for every thread of the CTA
+    if (valid) {
+      const uint8_t* st = smem + (c & 1) * stage_bytes;
+      const float4* xs = reinterpret_cast<const float4*>(st);
+      const int c0 = c * kChunk;
+      const int cols = min(kChunk, a.k - c0);  // a multiple of 32
+      if (QT == MLB_F32) {
+        const float4* wrow =
+            reinterpret_cast<const float4*>(a.w + j * a.row_bytes) + (c0 >> 2);
+        for (int q = lane; q < (cols >> 2); q += 32) {
+          const float4 w = __ldg(wrow + q);
 #pragma unroll
-        for (int t = 0; t < T; ++t) acc[t] = Dot4(w, xs[t * (kChunk / 4) + c], acc[t]);
-      }
-    } else {
-      const uint8_t* blocks = mine + (start - window);
-      for (int bl = lane; bl < (cols >> 5); bl += 32) {
-        const uint8_t* blk = blocks + bl * kBB;
-        const uint32_t scale = QT == MLB_Q4_1
-                                   ? *reinterpret_cast<const uint32_t*>(blk)
-                                   : Smem16(blk);
-        float part[T], xsum[T];
-#pragma unroll
-        for (int t = 0; t < T; ++t) part[t] = xsum[t] = 0.0f;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const float4 q = QuantValues<QT>(blk, g * 4);
+          for (int t = 0; t < T; ++t) acc[t] = Dot4(w, xs[t * (kChunk / 4) + q], acc[t]);
+        }
+      } else {
+        // Lane l takes float4 group o = l, l + 32, ...: 4 values of block
+        // o / 8.  Consecutive lanes read consecutive x float4s (no bank
+        // conflicts) and 8 lanes share one block's scale.
+        const uint8_t* blocks = st + T * kChunk * 4 + warp * slice + lead;
+        for (int o = lane; o < (cols >> 2); o += 32) {
+          const uint8_t* blk = blocks + (o >> 3) * kBB;
+          const float4 q = QuantValues<QT>(blk, (o & 7) * 4);
+          const uint32_t scale = QT == MLB_Q4_1
+                                     ? *reinterpret_cast<const uint32_t*>(blk)
+                                     : Smem16(blk);
+          const float d = Fp16BitsToF32(scale & 0xffffu);
 #pragma unroll
           for (int t = 0; t < T; ++t) {
-            const float4 xv = xs[t * (kChunk / 4) + bl * 8 + g];
-            part[t] = Dot4(q, xv, part[t]);
-            if (QT == MLB_Q4_1) xsum[t] += (xv.x + xv.y) + (xv.z + xv.w);
+            const float4 xv = xs[t * (kChunk / 4) + o];
+            acc[t] = fmaf(d, Dot4(q, xv, 0.0f), acc[t]);
+            if (QT == MLB_Q4_1)
+              acc[t] = fmaf(Fp16BitsToF32(scale >> 16),
+                            (xv.x + xv.y) + (xv.z + xv.w), acc[t]);
           }
-        }
-        const float d = Fp16BitsToF32(scale & 0xffffu);
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          acc[t] = fmaf(d, part[t], acc[t]);
-          if (QT == MLB_Q4_1) acc[t] = fmaf(Fp16BitsToF32(scale >> 16), xsum[t], acc[t]);
         }
       }
     }
+    __syncthreads();  // stage c & 1 is free for chunk c + 2
+    lead = next_lead;
   }
+  CopyAsyncWait<0>();
   if (!valid) return;
 #pragma unroll
   for (int t = 0; t < T; ++t) {
     const float s = WarpSum(acc[t]);
     if (lane == t) a.y[static_cast<int64_t>(t) * a.n + j] = s;
   }
+}
+
+// Streaming form, used when x for all T tokens fits in shared memory:
+// persistent CTAs copy x once; then every warp walks its rows segment by
+// segment (kChunk columns each) through a ring of kStages per-warp buffers
+// filled by cp.async kStages - 1 segments ahead.  No CTA-wide barrier sits
+// on the weight stream, so each warp keeps ~3 segments of weights in flight.
+constexpr int kStages = 4;
+constexpr int64_t kMaxResidentX = 96 * 1024;  // bytes of x kept in smem
+constexpr int64_t kMaxStreamSmem = 200 * 1024; // whole CTA (227 KB is the cap)
+
+template <int QT, int T>
+__global__ void __launch_bounds__(256) GemvStreamKernel(GemvArgs a, int slice,
+                                                        int rows_per_warp) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int k4 = a.k >> 2;
+  float4* xs = reinterpret_cast<float4*>(smem);
+  uint8_t* ring = smem + static_cast<size_t>(T) * a.k * 4 +
+                  static_cast<size_t>(warp) * kStages * slice;
+  // x for every token, once per CTA
+  const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  for (int i = threadIdx.x; i < T * k4; i += blockDim.x) CopyAsync16(xs + i, x4 + i);
+  CopyAsyncCommit();
+  CopyAsyncWait<0>();
+  __syncthreads();
+
+  const int nseg = (a.k + kChunk - 1) / kChunk;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + warp) *
+                       rows_per_warp;
+  int64_t rows = a.n - row0;
+  if (rows > rows_per_warp) rows = rows_per_warp;
+  const int items = rows > 0 ? static_cast<int>(rows) * nseg : 0;
+
+  // byte offset of item i's segment in the weight table
+  auto seg_start = [&](int i) -> int64_t {
+    const int64_t j = row0 + i / nseg;
+    const int sg = i % nseg;
+    return j * a.row_bytes + (QT == MLB_F32 ? static_cast<int64_t>(sg) * kChunk * 4
+                                            : static_cast<int64_t>(sg) * 32 * kBB);
+  };
+  auto seg_bytes = [&](int i) -> int64_t {
+    const int cols = min(kChunk, a.k - (i % nseg) * kChunk);
+    return QT == MLB_F32 ? static_cast<int64_t>(cols) * 4
+                         : static_cast<int64_t>(cols / 32) * kBB;
+  };
+  auto issue = [&](int i) {
+    uint8_t* dst = ring + (i % kStages) * slice;
+    const int64_t start = seg_start(i);
+    const int64_t window = start & ~int64_t{15};
+    const int n16 = static_cast<int>((start + seg_bytes(i) - window + 15) >> 4);
+    for (int q = lane; q < n16; q += 32) {
+      const int64_t off = window + 16 * static_cast<int64_t>(q);
+      if (off + 16 <= a.table_bytes) {
+        CopyAsync16(dst + 16 * q, a.w + off);
+      } else {
+        for (int b = 0; b < 16; ++b)
+          dst[16 * q + b] = off + b < a.table_bytes ? a.w[off + b] : 0;
+      }
+    }
+  };
+
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (i < items) issue(i);
+    CopyAsyncCommit();
+  }
+  float acc[T];
+#pragma unroll
+  for (int t = 0; t < T; ++t) acc[t] = 0.0f;
+  for (int i = 0; i < items; ++i) {
+    if (i + kStages - 1 < items) issue(i + kStages - 1);
+    CopyAsyncCommit();
+    CopyAsyncWait<kStages - 1>();  // item i's copies (this lane's) landed
+    __syncwarp();                  // ... and every lane's
+    const int sg = i % nseg;
+    const int c4 = min(kChunk, a.k - sg * kChunk) >> 2;
+    const int64_t start = seg_start(i);
+    const uint8_t* seg = ring + (i % kStages) * slice + (start & 15);
+    const float4* xseg = xs + sg * (kChunk / 4);
+    if (QT == MLB_F32) {
+      const float4* w4 = reinterpret_cast<const float4*>(seg);
+      for (int o = lane; o < c4; o += 32) {
+        const float4 w = w4[o];
+#pragma unroll
+        for (int t = 0; t < T; ++t) acc[t] = Dot4(w, xseg[t * k4 + o], acc[t]);
+      }
+    } else {
+      for (int o = lane; o < c4; o += 32) {
+        const uint8_t* blk = seg + (o >> 3) * kBB;
+        const float4 q = QuantValues<QT>(blk, (o & 7) * 4);
+        const uint32_t scale = QT == MLB_Q4_1
+                                   ? *reinterpret_cast<const uint32_t*>(blk)
+                                   : Smem16(blk);
+        const float d = Fp16BitsToF32(scale & 0xffffu);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 xv = xseg[t * k4 + o];
+          acc[t] = fmaf(d, Dot4(q, xv, 0.0f), acc[t]);
+          if (QT == MLB_Q4_1)
+            acc[t] = fmaf(Fp16BitsToF32(scale >> 16), (xv.x + xv.y) + (xv.z + xv.w),
+                          acc[t]);
+        }
+      }
+    }
+    if (sg == nseg - 1) {
+      const int64_t j = row0 + i / nseg;
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const float sum = WarpSum(acc[t]);
+        if (lane == t) a.y[static_cast<int64_t>(t) * a.n + j] = sum;
+        acc[t] = 0.0f;
+      }
+    }
+    __syncwarp();  // the slot is read by every lane before it is refilled
+  }
+  CopyAsyncWait<0>();
 }
 
 // Any k / alignment: one thread per output element, the reference's
@@ -211,16 +358,71 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Opts a kernel in to more than 48 KB of dynamic shared memory (two stages
+// of up to 8 x 4 KB of x plus 8 weight slices need up to 82 KB).
+template <typename K>
+bool AllowSmem(K kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return true;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(bytes)) == cudaSuccess;
+}
+
+template <int QT, int T>
+int LaunchStream(const GemvArgs& a, cudaStream_t s) {
+  constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
+  const int seg = QT == MLB_F32 ? kChunk * 4 : 32 * kBB;
+  const int slice = (seg + 15 + 15) / 16 * 16;
+  const size_t shm = static_cast<size_t>(T) * a.k * 4 +
+                     static_cast<size_t>(kWarpsPerCta) * kStages * slice;
+  auto kernel = GemvStreamKernel<QT, T>;
+  if (!AllowSmem(kernel, shm))
+    return Fail(MLB_ERR_CUDA, "mlb_linear_f32: shared memory opt-in");
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, shm) !=
+          cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  // spread rows evenly: every warp gets rows_per_warp consecutive rows
+  const int64_t max_warps = static_cast<int64_t>(per_sm) * SmCount() * kWarpsPerCta;
+  const int64_t rows_per_warp = (a.n + max_warps - 1) / max_warps;
+  const int64_t warps = (a.n + rows_per_warp - 1) / rows_per_warp;
+  const int64_t blocks = (warps + kWarpsPerCta - 1) / kWarpsPerCta;
+  kernel<<<static_cast<unsigned>(blocks), 256, shm, s>>>(a, slice,
+                                                        static_cast<int>(rows_per_warp));
+  return CheckLaunch("mlb_linear_f32");
+}
+
 template <int QT>
 int LaunchVec(const GemvArgs& a, int t_rows, cudaStream_t s) {
   constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
+  const int64_t ring = static_cast<int64_t>(kWarpsPerCta) * kStages *
+                       (((QT == MLB_F32 ? kChunk * 4 : 32 * kBB) + 30) / 16 * 16);
+  const int64_t x_bytes = static_cast<int64_t>(t_rows) * a.k * 4;
+  if (x_bytes <= kMaxResidentX && x_bytes + ring <= kMaxStreamSmem) {
+    switch (t_rows) {
+      case 1: return LaunchStream<QT, 1>(a, s);
+      case 2: return LaunchStream<QT, 2>(a, s);
+      case 3: return LaunchStream<QT, 3>(a, s);
+      case 4: return LaunchStream<QT, 4>(a, s);
+      case 5: return LaunchStream<QT, 5>(a, s);
+      case 6: return LaunchStream<QT, 6>(a, s);
+      case 7: return LaunchStream<QT, 7>(a, s);
+      case 8: return LaunchStream<QT, 8>(a, s);
+    }
+  }
   const int slice = QT == MLB_F32 ? 0 : (32 * kBB + 15 + 15) / 16 * 16;
-  const size_t shm = static_cast<size_t>(t_rows) * kChunk * 4 +
-                     static_cast<size_t>(slice) * kWarpsPerCta;
+  const size_t shm = 2 * (static_cast<size_t>(t_rows) * kChunk * 4 +
+                          static_cast<size_t>(slice) * kWarpsPerCta);
   const dim3 grid(static_cast<unsigned>((a.n + kWarpsPerCta - 1) / kWarpsPerCta));
   switch (t_rows) {
-#define MLB_T(N) \
-  case N: GemvKernel<QT, N><<<grid, 256, shm, s>>>(a, slice); break;
+#define MLB_T(N)                                                     \
+  case N:                                                            \
+    if (!AllowSmem(GemvKernel<QT, N>, shm))                          \
+      return Fail(MLB_ERR_CUDA, "mlb_linear_f32: shared memory opt-in"); \
+    GemvKernel<QT, N><<<grid, 256, shm, s>>>(a, slice);              \
+    break;
     MLB_T(1) MLB_T(2) MLB_T(3) MLB_T(4) MLB_T(5) MLB_T(6) MLB_T(7) MLB_T(8)
 #undef MLB_T
     default: return Fail(MLB_ERR_ARG, "mlb_linear_f32: bad token group");

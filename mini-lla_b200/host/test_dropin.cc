@@ -20,8 +20,10 @@
 #include <string>
 #include <vector>
 
+#include "mini_llama/cuda_attention.h"
 #include "mini_llama/cuda_layer_ops.h"
 #include "mini_llama/cuda_matmul.h"
+#include "mini_llama/kv_cache.h"
 #include "mini_llama/cuda_ops.h"
 #include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
@@ -354,6 +356,66 @@ void TestLinear(std::mt19937& rng) {
   Expect(Throws([&] { CudaLinear(CudaTensor({63}), dw); }), "CudaLinear size mismatch throws");
 }
 
+// CudaKvCache + CudaAttention against AttentionHead (forward.cc:50-67, in an
+// anonymous namespace there, so its loop is restated over the reference's
+// own KvCache and Softmax).
+void TestAttention(std::mt19937& rng) {
+  struct Case { int n_heads, n_kv, hd, layers, max_seq, position; };
+  for (const Case& c : {Case{8, 2, 64, 2, 64, 37}, Case{32, 8, 128, 1, 512, 300},
+                        Case{14, 2, 64, 3, 300, 255}, Case{4, 4, 32, 1, 8, 0}}) {
+    KvCache host(c.layers, c.max_seq, c.n_kv, c.hd);
+    CudaKvCache cache;
+    cache.Reset(c.layers, c.max_seq, c.n_kv, c.hd);
+    const int layer = c.layers - 1;
+    for (int t = 0; t <= c.position; ++t) {
+      const Tensor k = Random({c.n_kv, c.hd}, rng);
+      const Tensor v = Random({c.n_kv, c.hd}, rng);
+      host.Write(layer, t, k, v);
+      cache.Write(layer, t, CudaTensor::FromHost(k.Reshape({c.n_kv * c.hd})),
+                  CudaTensor::FromHost(v.Reshape({c.n_kv * c.hd})));
+    }
+    const Tensor q = Random({c.n_heads, c.hd}, rng);
+    const Tensor got = CudaAttention(CudaTensor::FromHost(q.Reshape({c.n_heads * c.hd})),
+                                     cache, layer, c.position, c.n_heads, c.n_kv, c.hd)
+                           .Download();
+    const int group = c.n_heads / c.n_kv;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(c.hd));
+    bool ok = true;
+    for (int head = 0; head < c.n_heads; ++head) {
+      Tensor scores({c.position + 1});
+      for (int t = 0; t <= c.position; ++t) {
+        const float* key = host.KeyPtr(layer, t, head / group);
+        float dot = 0.0f;
+        for (int i = 0; i < c.hd; ++i) dot += q.data[head * c.hd + i] * key[i];
+        scores.data[t] = dot * scale;
+      }
+      const Tensor w = Softmax(scores);
+      for (int i = 0; i < c.hd; ++i) {
+        float want = 0.0f;
+        double mag = 0.0;
+        for (int t = 0; t <= c.position; ++t) {
+          const float value = host.ValuePtr(layer, t, head / group)[i];
+          want += w.data[t] * value;
+          mag += w.data[t] * std::fabs(value);
+        }
+        ok = ok && std::fabs(double(got.data[head * c.hd + i]) - want) <= 1e-5 * mag + 1e-30;
+      }
+    }
+    Expect(ok, "CudaAttention heads=" + std::to_string(c.n_heads) +
+                   " pos=" + std::to_string(c.position));
+    std::vector<float> keys_back(static_cast<size_t>(c.n_kv) * c.hd);
+    cudaMemcpy(keys_back.data(),
+               cache.Keys(layer) + static_cast<size_t>(c.position) * c.n_kv * c.hd,
+               keys_back.size() * sizeof(float), cudaMemcpyDeviceToHost);
+    Expect(std::memcmp(keys_back.data(), host.KeyPtr(layer, c.position, 0),
+                       keys_back.size() * sizeof(float)) == 0,
+           "CudaKvCache::Write copies bit-exact");
+    Expect(Throws([&] { cache.Write(layer, c.max_seq, CudaTensor({c.n_kv * c.hd}),
+                                    CudaTensor({c.n_kv * c.hd})); }),
+           "CudaKvCache::Write out of range throws");
+  }
+}
+
 // One host thread per "device" entry; a single-GPU box lists device 0 twice
 // (independent token ranges, no waits between them).
 void TestShardingAndWaits(std::mt19937& rng) {
@@ -434,6 +496,7 @@ int main() {
     TestBatched(rng);
     TestShardingAndWaits(rng);
     TestLinear(rng);
+    TestAttention(rng);
     TestRuntime();
   } catch (const std::exception& e) {
     std::printf("FAIL: unexpected exception: %s\n", e.what());

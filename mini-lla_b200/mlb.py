@@ -52,6 +52,12 @@ SIGNATURES = {
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
     "mlb_linear_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                c_int64, c_void_p, c_void_p]),
+    "mlb_kv_write_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                 c_int64, c_int64, c_int, c_int, c_void_p]),
+    "mlb_attention_scratch_floats": (c_int64, [c_int, c_int, c_int, c_int64]),
+    "mlb_attention_decode_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_int64, c_int64, c_int, c_int, c_int,
+                                         c_void_p, c_int64, c_void_p]),
 }
 
 _lib = None
@@ -316,6 +322,50 @@ def linear(weight, qtype: int, n: int, k: int, x, out=None, stream=None):
         out = torch.empty(shape, dtype=torch.float32, device=x.device)
     _check(load().mlb_linear_f32(_ptr(weight), qtype, n, k, _ptr(x), t_rows,
                                  _ptr(out), _stream(stream)), op)
+    return out
+
+
+def kv_write(keys, values, k, v, position: int, stream=None):
+    """Writes k, v [rows, kv_heads, hd] at positions [position, +rows) of one
+    layer's cache keys/values [max_seq, kv_heads, hd]."""
+    op = "kv_write"
+    for t, name in ((keys, "keys"), (values, "values"), (k, "k"), (v, "v")):
+        _f32_cuda(t, op, name)
+    _require(keys.shape == values.shape and keys.dim() == 3, op,
+             "cache must be [max_seq, kv_heads, head_dim]")
+    max_seq, kvh, hd = keys.shape
+    _require(k.numel() == v.numel() and k.numel() % (kvh * hd) == 0, op,
+             "k/v shape mismatch")
+    rows = k.numel() // (kvh * hd)
+    _check(load().mlb_kv_write_f32(_ptr(keys), _ptr(values), _ptr(k), _ptr(v),
+                                   int(position), rows, max_seq, kvh, hd,
+                                   _stream(stream)), op)
+
+
+def attention_scratch_floats(n_heads: int, n_kv_heads: int, head_dim: int,
+                             position: int) -> int:
+    return int(load().mlb_attention_scratch_floats(n_heads, n_kv_heads,
+                                                   head_dim, position))
+
+
+def attention_decode(q, keys, values, position: int, out=None, scratch=None,
+                     stream=None):
+    """Decode attention of q [n_heads, hd] at `position` over one layer's
+    cache [max_seq, kv_heads, hd] -> [n_heads, hd]."""
+    import torch
+    op = "attention_decode"
+    for t, name in ((q, "q"), (keys, "keys"), (values, "values")):
+        _f32_cuda(t, op, name)
+    max_seq, kvh, hd = keys.shape
+    nh = q.numel() // hd
+    if out is None:
+        out = torch.empty((nh, hd), dtype=torch.float32, device=q.device)
+    need = attention_scratch_floats(nh, kvh, hd, position)
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.float32, device=q.device)
+    _check(load().mlb_attention_decode_f32(
+        _ptr(q), _ptr(keys), _ptr(values), _ptr(out), int(position), max_seq,
+        nh, kvh, hd, _ptr(scratch), scratch.numel(), _stream(stream)), op)
     return out
 
 

@@ -16,6 +16,7 @@ from typing import Optional
 
 F32, Q8_0, Q4_0, Q4_1 = 0, 1, 2, 3
 QNAME = {F32: "F32", Q8_0: "Q8_0", Q4_0: "Q4_0", Q4_1: "Q4_1"}
+QTYPE_BY_NAME = {v: k for k, v in QNAME.items()}
 BLOCK_BYTES = {F32: 128, Q8_0: 34, Q4_0: 18, Q4_1: 20}
 
 

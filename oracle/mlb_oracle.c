@@ -321,3 +321,36 @@ void mlbo_linear_rows(const void* table, int qtype, int64_t n, int64_t k,
     }
   }
 }
+
+/* Decode attention of one token at `position` over one layer's cache
+ * [max_seq, n_kv_heads, hd]; reference src/forward.cc:50-95 (AttentionHead,
+ * Attention): per query head h (kv head h / group), score_t = dot(q, k_t) *
+ * scale with a sequential dot and scale = 1 / sqrt(hd) (forward.cc:75),
+ * w = Softmax(score) (ops.cc:83-98), out[i] += w_t * v_t[i] in t order.
+ * scores must hold position + 1 floats. */
+void mlbo_attention_decode(const float* q, const float* keys,
+                           const float* values, float* out, int64_t position,
+                           int n_heads, int n_kv_heads, int hd, float* scores) {
+  const int group = n_heads / n_kv_heads;
+  const float scale = 1.0f / sqrtf((float)hd);
+  const int64_t visible = position + 1;
+  const int64_t stride = (int64_t)n_kv_heads * hd;
+  for (int h = 0; h < n_heads; ++h) {
+    const int kvh = h / group;
+    const float* qh = q + (int64_t)h * hd;
+    for (int64_t t = 0; t < visible; ++t) {
+      const float* key = keys + t * stride + (int64_t)kvh * hd;
+      float dot = 0.0f;
+      for (int i = 0; i < hd; ++i) dot += qh[i] * key[i];
+      scores[t] = dot * scale;
+    }
+    mlbo_softmax_row(scores, scores, visible);
+    float* oh = out + (int64_t)h * hd;
+    for (int i = 0; i < hd; ++i) oh[i] = 0.0f;
+    for (int64_t t = 0; t < visible; ++t) {
+      const float* value = values + t * stride + (int64_t)kvh * hd;
+      const float w = scores[t];
+      for (int i = 0; i < hd; ++i) oh[i] += w * value[i];
+    }
+  }
+}

@@ -60,6 +60,9 @@ class Oracle:
             "mlbo_rope_table": (None, [c_float, c_int, c_int64, c_int64, c_void_p]),
             "mlbo_linear_rows": (None, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                         c_int64, c_void_p]),
+            "mlbo_attention_decode": (None, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                             c_int64, c_int, c_int, c_int,
+                                             c_void_p]),
             "mlbo_rope_rows": (c_int64, [c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_int64, c_int, c_int, c_int,
                                          c_float, c_int]),
@@ -132,6 +135,18 @@ class Oracle:
                                   _p(x), t_rows, _p(y))
         return y
 
+    def attention_decode(self, q, keys, values, position, n_heads, n_kv_heads):
+        """q [n_heads, hd]; keys/values [>= position+1, n_kv_heads, hd]."""
+        q = _f32(q)
+        hd = q.size // n_heads
+        keys, values = _f32(keys), _f32(values)
+        out = np.empty((n_heads, hd), np.float32)
+        scores = np.empty(position + 1, np.float32)
+        self.lib.mlbo_attention_decode(_p(q), _p(keys), _p(values), _p(out),
+                                       position, n_heads, n_kv_heads, hd,
+                                       _p(scores))
+        return out
+
     def rope_table(self, theta, hd, pos_begin, pos_end):
         out = np.empty((pos_end - pos_begin, hd), dtype=np.float32)
         self.lib.mlbo_rope_table(theta, hd, pos_begin, pos_end, _p(out))
@@ -172,6 +187,8 @@ class Reference:
                                              c_int64, V]),
             "mlref_quantize": (c_int, [V, c_int64, c_int64, c_int, V]),
             "mlref_linear": (c_int, [V, c_int, c_int64, c_int64, V, c_int64, V]),
+            "mlref_attention_decode": (c_int, [V, V, V, V, c_int64, c_int, c_int,
+                                               c_int]),
             "mlref_rows_new": (V, [V, c_int64, c_int64]),
             "mlref_heads_new": (V, [V, c_int64, c_int, c_int]),
             "mlref_rows_free": (None, [V]),
@@ -253,6 +270,16 @@ class Reference:
                                    _p(x), t_rows, _p(y))
         assert rc == 0, rc
         return y
+
+    def attention_decode(self, q, keys, values, position, n_heads, n_kv_heads):
+        q = _f32(q)
+        hd = q.size // n_heads
+        out = np.empty((n_heads, hd), np.float32)
+        rc = self.lib.mlref_attention_decode(_p(q), _p(_f32(keys)), _p(_f32(values)),
+                                             _p(out), position, n_heads,
+                                             n_kv_heads, hd)
+        assert rc == 0, rc
+        return out
 
     def quantize(self, values, qtype, row_bytes):
         values = _f32(values)

@@ -12,12 +12,14 @@
 //      as reference Tensors outside the timed region.
 // It is never linked into, or called by, the product library.
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
 #include <stdexcept>
 #include <vector>
 
+#include "mini_llama/kv_cache.h"
 #include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
 #include "mini_llama/quantized_tensor.h"
@@ -196,6 +198,47 @@ int mlref_linear(const void* table, int qtype, int64_t n, int64_t k,
     std::memcpy(input.data.data(), x, 4 * t_rows * k);
     const Tensor out = mini_lla::Linear(input, w);
     std::memcpy(y, out.data.data(), 4 * t_rows * n);
+  });
+}
+
+// Decode attention through the reference's KvCache (kv_cache.cc) and
+// Softmax (ops.cc).  AttentionHead of src/forward.cc:50-67 sits in an
+// anonymous namespace there; this is its loop, step for step, over the
+// reference's own cache accessors.  keys/values: [visible, kv_heads, hd].
+int mlref_attention_decode(const float* q, const float* keys,
+                           const float* values, float* out, int64_t position,
+                           int n_heads, int n_kv_heads, int hd) {
+  return Guard([&] {
+    const int visible = static_cast<int>(position) + 1;
+    mini_lla::KvCache cache(1, visible, n_kv_heads, hd);
+    for (int t = 0; t < visible; ++t) {
+      Tensor k({n_kv_heads, hd}), v({n_kv_heads, hd});
+      std::memcpy(k.data.data(), keys + static_cast<size_t>(t) * n_kv_heads * hd,
+                  4 * n_kv_heads * hd);
+      std::memcpy(v.data.data(), values + static_cast<size_t>(t) * n_kv_heads * hd,
+                  4 * n_kv_heads * hd);
+      cache.Write(0, t, k, v);
+    }
+    const int group = n_heads / n_kv_heads;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    for (int head = 0; head < n_heads; ++head) {
+      const int kv_head = head / group;
+      Tensor scores({visible});
+      for (int t = 0; t < visible; ++t) {
+        const float* key = cache.KeyPtr(0, t, kv_head);
+        float dot = 0.0f;
+        for (int i = 0; i < hd; ++i) dot += q[head * hd + i] * key[i];
+        scores.data[static_cast<size_t>(t)] = dot * scale;
+      }
+      const Tensor weights = mini_lla::Softmax(scores);
+      float* output = out + head * hd;
+      for (int i = 0; i < hd; ++i) output[i] = 0.0f;
+      for (int t = 0; t < visible; ++t) {
+        const float* value = cache.ValuePtr(0, t, kv_head);
+        const float weight = weights.data[static_cast<size_t>(t)];
+        for (int i = 0; i < hd; ++i) output[i] += weight * value[i];
+      }
+    }
   });
 }
 

@@ -24,26 +24,30 @@ def test_cuda_forward_links_against_this_layer():
     fwd = os.path.join(REF, "cuda_forward.o")
     ops = os.path.join(REF, "cuda_ops_host.o")
     if not all(os.path.exists(p) for p in
-               (fwd, ops, os.path.join(REF, "cuda_matmul_host.o"))):
+               (fwd, ops, os.path.join(REF, "cuda_matmul_host.o"),
+                os.path.join(REF, "cuda_attention_host.o"))):
         pytest.skip("drop-in objects not built (reference headers absent)")
     undefined = subprocess.run(["nm", "-C", "--undefined-only", fwd], check=True,
                                capture_output=True, text=True).stdout
     needed = {l.split("U ", 1)[1].strip() for l in undefined.splitlines()
               if "U mini_lla::Cuda" in l}
     have = set()
-    for obj in (ops, os.path.join(REF, "cuda_matmul_host.o")):
+    for obj in (ops, os.path.join(REF, "cuda_matmul_host.o"),
+                os.path.join(REF, "cuda_attention_host.o")):
         defined = subprocess.run(["nm", "-C", "--defined-only", obj], check=True,
                                  capture_output=True, text=True).stdout
         have |= {l.split(" ", 2)[2].strip() for l in defined.splitlines()
                  if " T mini_lla::Cuda" in l}
-    # the operator entry points cuda_forward.cc calls (cuda_ops.h:11-34) and
-    # its linear layer (cuda_matmul.h:11)
+    # the operator entry points cuda_forward.cc calls (cuda_ops.h:11-34), its
+    # linear layer (cuda_matmul.h:11) and its KV cache + attention
+    # (cuda_attention.h:8-45)
     ops_needed = {n for n in needed if n.split("(")[0] in {
         "mini_lla::CudaRmsNorm", "mini_lla::CudaRope", "mini_lla::CudaSilu",
         "mini_lla::CudaMul", "mini_lla::CudaAdd", "mini_lla::CudaSoftmax",
         "mini_lla::CudaEmbeddingRow", "mini_lla::CudaAddBias",
-        "mini_lla::CudaLinear"}}
-    assert len(ops_needed) >= 7, needed
+        "mini_lla::CudaLinear", "mini_lla::CudaAttention",
+        "mini_lla::CudaKvCache::Write", "mini_lla::CudaKvCache::Reset"}}
+    assert len(ops_needed) >= 10, needed
     missing = ops_needed - have
     assert not missing, f"cuda_ops.cc lacks {missing}"
 

@@ -1,0 +1,102 @@
+"""Decode attention and the KV-cache write through the C ABI, against the
+reference arithmetic of src/forward.cc:50-95 (restated in the oracle and
+pinned against the reference's KvCache + Softmax in tests/test_oracle.py).
+
+Attention sums run in another order (split positions, online softmax), so
+each output is checked within 1e-5 * sum_t w_t |v_t[i]| — the size of the
+terms it sums; the cache write is a copy and must be bit-exact.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_bitexact
+
+import mlb
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, device):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _magnitude(q, keys, values, position, n_heads, n_kv):
+    hd = q.shape[1]
+    group = n_heads // n_kv
+    out = np.empty((n_heads, hd))
+    for h in range(n_heads):
+        k = keys[:position + 1, h // group].astype(np.float64)
+        v = values[:position + 1, h // group].astype(np.float64)
+        s = k @ q[h].astype(np.float64) / np.sqrt(hd)
+        w = np.exp(s - s.max())
+        w /= w.sum()
+        out[h] = w @ np.abs(v)
+    return out
+
+
+@pytest.mark.parametrize("nh,nkv,hd,pos,max_seq", [
+    (4, 2, 8, 0, 16), (8, 2, 64, 37, 64), (32, 8, 128, 300, 512),
+    (14, 2, 64, 255, 256), (32, 32, 128, 2047, 2048), (28, 4, 128, 4095, 4096),
+    (8, 1, 256, 1000, 1024), (16, 2, 32, 9999, 10000), (64, 8, 128, 65, 70)])
+def test_attention_decode_vs_oracle(cuda, oracle, nh, nkv, hd, pos, max_seq):
+    import torch
+    rng = np.random.default_rng(nh * 1000 + pos)
+    q = rng.standard_normal((nh, hd), dtype=np.float32)
+    keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    values = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    want = oracle.attention_decode(q, keys, values, pos, nh, nkv)
+    got = mlb.attention_decode(dev(q, cuda), dev(keys, cuda), dev(values, cuda), pos)
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    mag = _magnitude(q, keys, values, pos, nh, nkv)
+    err = np.abs(got.astype(np.float64) - want)
+    ratio = float((err / np.maximum(mag, 1e-30)).max())
+    assert ratio <= 1e-5, f"max error / magnitude {ratio:.2e}"
+
+
+def test_attention_reuses_scratch_and_rejects_bad_input(cuda, oracle):
+    import torch
+    rng = np.random.default_rng(4)
+    nh, nkv, hd, max_seq = 8, 2, 64, 300
+    keys = dev(rng.standard_normal((max_seq, nkv, hd), dtype=np.float32), cuda)
+    values = dev(rng.standard_normal((max_seq, nkv, hd), dtype=np.float32), cuda)
+    need = mlb.attention_scratch_floats(nh, nkv, hd, max_seq - 1)
+    scratch = torch.empty(need, device=cuda)
+    for pos in (0, 1, 150, max_seq - 1):
+        q = rng.standard_normal((nh, hd), dtype=np.float32)
+        got = mlb.attention_decode(dev(q, cuda), keys, values, pos, scratch=scratch)
+        want = oracle.attention_decode(q, keys.cpu().numpy(), values.cpu().numpy(),
+                                       pos, nh, nkv)
+        assert np.allclose(got.cpu().numpy(), want, rtol=0, atol=1e-5)
+    with pytest.raises(IndexError):
+        mlb.attention_decode(dev(q, cuda), keys, values, max_seq)
+    with pytest.raises(ValueError):
+        mlb.attention_decode(dev(q, cuda), keys, values, 10,
+                             scratch=torch.empty(1, device=cuda))
+    with pytest.raises(ValueError):   # 8 heads over 3 kv heads
+        bad = torch.zeros((max_seq, 3, hd), device=cuda)
+        mlb.attention_decode(dev(q, cuda), bad, bad, 10)
+
+
+def test_kv_write_is_a_copy(cuda):
+    import torch
+    rng = np.random.default_rng(5)
+    max_seq, nkv, hd = 50, 4, 32
+    keys = torch.zeros((max_seq, nkv, hd), device=cuda)
+    values = torch.zeros((max_seq, nkv, hd), device=cuda)
+    k1 = rng.standard_normal((nkv, hd), dtype=np.float32)
+    v1 = rng.standard_normal((nkv, hd), dtype=np.float32)
+    mlb.kv_write(keys, values, dev(k1, cuda), dev(v1, cuda), 7)
+    kb = rng.standard_normal((5, nkv, hd), dtype=np.float32)
+    vb = rng.standard_normal((5, nkv, hd), dtype=np.float32)
+    mlb.kv_write(keys, values, dev(kb, cuda), dev(vb, cuda), 45)
+    torch.cuda.synchronize()
+    kh, vh = keys.cpu().numpy(), values.cpu().numpy()
+    assert_bitexact(kh[7], k1)
+    assert_bitexact(vh[7], v1)
+    assert_bitexact(kh[45:50], kb)
+    assert_bitexact(vh[45:50], vb)
+    assert not kh[:7].any() and not kh[8:45].any()
+    with pytest.raises(IndexError):
+        mlb.kv_write(keys, values, dev(kb, cuda), dev(vb, cuda), 46)
