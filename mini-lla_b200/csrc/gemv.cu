@@ -26,6 +26,8 @@
 // HBM roofline per launch: n * row_bytes (weights) + 4 * T * (k + n).
 #include <climits>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace mlb {
@@ -49,15 +51,23 @@ __device__ __forceinline__ uint32_t Smem16(const uint8_t* p) {
   return *reinterpret_cast<const unsigned short*>(p);
 }
 
-// Four quant values of one block (elements e..e+3), as floats.
+// Four bytes -> four exact floats without I2F (a quarter-rate pipe): each
+// byte goes into the low mantissa bits of 2^23 with a byte permute, and one
+// subtract removes 2^23 (plus the byte bias).  `bias` = 2^23 + 128 for signed
+// int8 stored as b ^ 0x80, 2^23 for 4-bit values, 2^23 + 8 for Q4_0's n - 8.
+__device__ __forceinline__ float4 BytesToFloat4(uint32_t u, float bias) {
+  return make_float4(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - bias,
+                     __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - bias,
+                     __int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - bias,
+                     __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - bias);
+}
+
+// Four quant values of one block (elements e..e+3), as exact floats.
 template <int QT>
 __device__ __forceinline__ float4 QuantValues(const uint8_t* blk, int e) {
   if (QT == MLB_Q8_0) {
     const uint32_t q = Smem16(blk + 2 + e) | (Smem16(blk + 4 + e) << 16);
-    return make_float4(static_cast<float>(static_cast<int8_t>(q & 0xffu)),
-                       static_cast<float>(static_cast<int8_t>((q >> 8) & 0xffu)),
-                       static_cast<float>(static_cast<int8_t>((q >> 16) & 0xffu)),
-                       static_cast<float>(static_cast<int8_t>(q >> 24)));
+    return BytesToFloat4(q ^ 0x80808080u, 8388736.0f);
   }
   uint32_t q;
   if (QT == MLB_Q4_0) {
@@ -66,11 +76,13 @@ __device__ __forceinline__ float4 QuantValues(const uint8_t* blk, int e) {
     q = *reinterpret_cast<const uint32_t*>(blk + 4 + (e & 15));
   }
   if (e >= 16) q >>= 4;
-  const float bias = QT == MLB_Q4_0 ? 8.0f : 0.0f;
-  return make_float4(static_cast<float>(q & 15u) - bias,
-                     static_cast<float>((q >> 8) & 15u) - bias,
-                     static_cast<float>((q >> 16) & 15u) - bias,
-                     static_cast<float>((q >> 24) & 15u) - bias);
+  return BytesToFloat4(q & 0x0F0F0F0Fu, QT == MLB_Q4_0 ? 8388616.0f : 8388608.0f);
+}
+
+// fp16 scale bits -> f32 with the hardware conversion (exact for every
+// non-NaN pattern; this path is checked to a tolerance, not bit for bit).
+__device__ __forceinline__ float HalfBits(uint32_t bits) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
 }
 
 __device__ __forceinline__ float Dot4(const float4& a, const float4& b, float acc) {
@@ -178,14 +190,13 @@ __global__ void __launch_bounds__(256) GemvKernel(GemvArgs a, int slice) {
           const uint32_t scale = QT == MLB_Q4_1
                                      ? *reinterpret_cast<const uint32_t*>(blk)
                                      : Smem16(blk);
-          const float d = Fp16BitsToF32(scale & 0xffffu);
+          const float d = HalfBits(scale & 0xffffu);
+          const float m = QT == MLB_Q4_1 ? HalfBits(scale >> 16) : 0.0f;
 #pragma unroll
           for (int t = 0; t < T; ++t) {
             const float4 xv = xs[t * (kChunk / 4) + o];
             acc[t] = fmaf(d, Dot4(q, xv, 0.0f), acc[t]);
-            if (QT == MLB_Q4_1)
-              acc[t] = fmaf(Fp16BitsToF32(scale >> 16),
-                            (xv.x + xv.y) + (xv.z + xv.w), acc[t]);
+            if (QT == MLB_Q4_1) acc[t] = fmaf(m, (xv.x + xv.y) + (xv.z + xv.w), acc[t]);
           }
         }
       }
@@ -295,14 +306,13 @@ __global__ void __launch_bounds__(256) GemvStreamKernel(GemvArgs a, int slice,
         const uint32_t scale = QT == MLB_Q4_1
                                    ? *reinterpret_cast<const uint32_t*>(blk)
                                    : Smem16(blk);
-        const float d = Fp16BitsToF32(scale & 0xffffu);
+        const float d = HalfBits(scale & 0xffffu);
+        const float m = QT == MLB_Q4_1 ? HalfBits(scale >> 16) : 0.0f;
 #pragma unroll
         for (int t = 0; t < T; ++t) {
           const float4 xv = xseg[t * k4 + o];
           acc[t] = fmaf(d, Dot4(q, xv, 0.0f), acc[t]);
-          if (QT == MLB_Q4_1)
-            acc[t] = fmaf(Fp16BitsToF32(scale >> 16), (xv.x + xv.y) + (xv.z + xv.w),
-                          acc[t]);
+          if (QT == MLB_Q4_1) acc[t] = fmaf(m, (xv.x + xv.y) + (xv.z + xv.w), acc[t]);
         }
       }
     }
