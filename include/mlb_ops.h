@@ -242,6 +242,30 @@ int mlb_attention_decode_f32(const float* q, const float* keys,
                              int64_t scratch_floats, void* stream);
 
 /*
+ * Decode attention that allocates nothing.  No counterpart in the reference:
+ * it is mlb_attention_decode_f32 for callers that cannot provide device
+ * scratch — a plugin inside a host framework that owns every device
+ * allocation, or a token loop that must not call cudaMalloc / cudaFree
+ * (those can synchronise the whole device).  The slice partials live in a
+ * file-scope device array of the library, 1 Mi floats (4 MiB), held on every
+ * GPU where the library's kernels are loaded until the process exits.
+ *   - Sizes whose mlb_attention_scratch_floats(...) exceeds 1 Mi floats are
+ *     rejected with MLB_ERR_ARG and a message naming the need.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before any
+ *     stream capture.
+ *   - Every call shares the one array and it keeps the last call's contents
+ *     (nothing in it needs to start at zero): calls that overlap on the GPU —
+ *     on different streams, or from several host threads — race.
+ * Arguments and results as for mlb_attention_decode_f32.
+ */
+int mlb_attention_decode_noalloc_f32(const float* q, const float* keys,
+                                     const float* values, float* out,
+                                     int64_t position, int64_t max_seq,
+                                     int n_heads, int n_kv_heads, int head_dim,
+                                     void* stream);
+
+/*
  * Helper for synchronous callers: waits for `stream`, copies the device
  * status word to the host, and returns MLB_OK when it is zero, MLB_ERR_RANGE
  * when a bit is set (the bits are stored in *bits_host when non-NULL), or

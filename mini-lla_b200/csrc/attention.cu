@@ -23,6 +23,8 @@
 // q and out.
 #include <climits>
 #include <cmath>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -327,4 +329,78 @@ extern "C" int mlb_kv_write_f32(float* keys, float* values, const float* k,
                   256, 0, AsStream(stream)>>>(keys, values, k, v, position * per,
                                               count);
   return CheckLaunch("mlb_kv_write_f32");
+}
+
+// ---------------------------------------------------------------------------
+// Attention without any allocation by the caller or the library.
+//
+// Some callers cannot hand the library device memory for scratch: a plugin
+// inside a host framework that owns every device allocation (its allocator,
+// its memory budget), or a token loop that must not call cudaMalloc /
+// cudaFree, which can synchronise the whole device.  For them the slice
+// partials live in this file-scope device array instead of caller scratch.
+// It is part of the library's device code: every GPU on which the library's
+// kernels are loaded holds it (4 MiB) until the process exits.
+namespace mlb {
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t{1} << 20;  // 4 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxNoAllocDevices = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_address[kMaxNoAllocDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name only stands in for the symbol, so the address is looked up
+// once per device (with that device current) and cached.
+int NoAllocScratch(float** out) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess)
+    return Fail(MLB_ERR_CUDA, std::string("attention (no alloc): ") + cudaGetErrorString(err));
+  if (device < 0 || device >= kMaxNoAllocDevices)
+    return Fail(MLB_ERR_ARG, "attention (no alloc): device index beyond 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[device] == nullptr) {
+    void* address = nullptr;
+    err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+    if (err != cudaSuccess || address == nullptr) {
+      cudaGetLastError();
+      return Fail(MLB_ERR_CUDA, std::string("attention (no alloc): scratch address: ") +
+                                    cudaGetErrorString(err));
+    }
+    g_noalloc_address[device] = static_cast<float*>(address);
+  }
+  *out = g_noalloc_address[device];
+  return MLB_OK;
+}
+
+}  // namespace
+}  // namespace mlb
+
+extern "C" int mlb_attention_decode_noalloc_f32(const float* q, const float* keys,
+                                                const float* values, float* out,
+                                                int64_t position, int64_t max_seq,
+                                                int n_heads, int n_kv_heads,
+                                                int head_dim, void* stream) {
+  using namespace mlb;
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || position < 0)
+    return Fail(MLB_ERR_ARG, "mlb_attention_decode_noalloc_f32: bad sizes");
+  const int64_t need = AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1);
+  if (need > kNoAllocScratchFloats) {
+    return Fail(MLB_ERR_ARG,
+                "mlb_attention_decode_noalloc_f32: these sizes need " +
+                    std::to_string(need) + " floats of scratch, more than the " +
+                    std::to_string(kNoAllocScratchFloats) +
+                    " (4 MiB) this entry point holds; use mlb_attention_decode_f32 "
+                    "with caller-provided scratch");
+  }
+  float* scratch = nullptr;
+  const int rc = NoAllocScratch(&scratch);
+  if (rc != MLB_OK) return rc;
+  // Every scratch slot the combine kernel reads is written first by the
+  // partial kernel of the same call, so nothing needs clearing.
+  return AttentionDecode(q, keys, values, out, position, max_seq, n_heads,
+                         n_kv_heads, head_dim, scratch, stream);
 }

@@ -58,6 +58,9 @@ SIGNATURES = {
     "mlb_attention_decode_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_int64, c_int64, c_int, c_int, c_int,
                                          c_void_p, c_int64, c_void_p]),
+    "mlb_attention_decode_noalloc_f32": (c_int, [c_void_p, c_void_p, c_void_p,
+                                                 c_void_p, c_int64, c_int64, c_int,
+                                                 c_int, c_int, c_void_p]),
 }
 
 _lib = None
