@@ -676,6 +676,43 @@ def linear_bench(args):
             torch.cuda.empty_cache()
 
 
+# ---------------------------------------------------------------- attention
+
+ATTENTION_CASES = (  # (name, n_heads, n_kv_heads, head_dim, position)
+    ("llama3-8b", 32, 8, 128, 2047), ("llama3-8b", 32, 8, 128, 16383),
+    ("llama-7b", 32, 32, 128, 2047), ("qwen2-0.5b", 14, 2, 64, 4095),
+    ("qwen2-7b", 28, 4, 128, 32767))
+
+
+def attention_bench(args):
+    """Decode attention (mlb_attention_decode_f32) of one token over one
+    layer's cache: one JSON line per case, GB/s over K + V bytes read."""
+    import torch
+    import mlb
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = measured_peak()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    for name, nh, nkv, hd, pos in ATTENTION_CASES:
+        keys = torch.randn((pos + 1, nkv, hd), generator=g, device=dev)
+        values = torch.randn((pos + 1, nkv, hd), generator=g, device=dev)
+        q = torch.randn((nh, hd), generator=g, device=dev)
+        out = torch.empty((nh, hd), device=dev)
+        scratch = torch.empty(mlb.attention_scratch_floats(nh, nkv, hd, pos), device=dev)
+        fn = lambda: mlb.attention_decode(q, keys, values, pos, out=out,  # noqa: E731
+                                          scratch=scratch)
+        nbytes = 8 * (pos + 1) * nkv * hd + 8 * nh * hd
+        ms = time_fn(fn, nbytes, 1)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "attention": name, "heads": nh, "kv_heads": nkv, "head_dim": hd,
+            "position": pos, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+            "frac_of_measured": round(gbs / peak, 4), "peak_kind": peak_kind,
+            "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}), flush=True)
+        del keys, values
+        torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------- sweep
 
 SWEEP_OPS = ("rmsnorm", "res_rmsnorm", "swiglu", "emb_q8_0", "emb_q4_0", "emb_q4_1")
@@ -837,6 +874,8 @@ def main():
                     help="bandwidth sweep: one JSON line per (op, H, T) point")
     ap.add_argument("--linear", action="store_true",
                     help="decode-path linear layer: one JSON line per shape")
+    ap.add_argument("--attention", action="store_true",
+                    help="decode attention: one JSON line per case")
     ap.add_argument("--linear-qtypes", default="", help="e.g. Q8_0,F32")
     ap.add_argument("--linear-shapes", default="", help="e.g. 14336x4096")
     ap.add_argument("--linear-tokens", default="", help="e.g. 1,4")
@@ -850,6 +889,9 @@ def main():
         return
     if args.linear:
         linear_bench(args)
+        return
+    if args.attention:
+        attention_bench(args)
         return
     if args.impl == "reference":
         reference_arm(args, cfg)

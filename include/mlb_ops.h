@@ -205,6 +205,15 @@ int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                    const float* x, int64_t t_rows, float* y, void* stream);
 
 /*
+ * Number of bounded device-side waits (a bulk weight copy that did not land
+ * within the kernel's poll limit) that gave up on the current device since
+ * the library was loaded.  A kernel that gives up leaves NaN in the outputs
+ * it did not finish instead of hanging.  Synchronous.  Diagnostic only: no
+ * counterpart in the reference.
+ */
+int mlb_wait_timeouts(unsigned int* count);
+
+/*
  * KV-cache write: rows tokens' k and v ([rows, n_kv_heads * head_dim]) go to
  * positions [position, position + rows) of one layer's cache, laid out as the
  * reference's CudaKvCache layer [max_seq, n_kv_heads, head_dim]
@@ -240,6 +249,29 @@ int mlb_attention_decode_f32(const float* q, const float* keys,
                              int64_t max_seq, int n_heads, int n_kv_heads,
                              int head_dim, float* scratch,
                              int64_t scratch_floats, void* stream);
+
+/* Floats of scratch mlb_attention_rows_f32 needs (-1 for bad arguments). */
+int64_t mlb_attention_rows_scratch_floats(int n_heads, int n_kv_heads,
+                                          int head_dim, int64_t position,
+                                          int64_t rows);
+
+/*
+ * Causal attention of `rows` consecutive query tokens (a prompt chunk) over
+ * one layer's cache: row r is the token at position + r and attends to cache
+ * positions 0 .. position + r, exactly as if the reference's per-token
+ * CudaAttention (cuda_attention.cu:147-195) were called for each row in
+ * order after its K/V were written.  This is the attention step of the
+ * row-batched prefill driver, which replaces ForwardBatch's per-token loop
+ * (batch.cc:26-41); write the rows' K/V first (mlb_kv_write_f32 with the same
+ * position and rows).  q, out: [rows, n_heads, head_dim]; other arguments and
+ * the tolerance as mlb_attention_decode_f32 (which is this call with
+ * rows = 1).  MLB_ERR_RANGE when position + rows > max_seq.
+ */
+int mlb_attention_rows_f32(const float* q, const float* keys,
+                           const float* values, float* out, int64_t position,
+                           int64_t rows, int64_t max_seq, int n_heads,
+                           int n_kv_heads, int head_dim, float* scratch,
+                           int64_t scratch_floats, void* stream);
 
 /*
  * Decode attention that allocates nothing.  No counterpart in the reference:

@@ -41,8 +41,8 @@ struct AttnArgs {
   const float* keys;
   const float* values;
   float* out;
-  float* scratch;  // [n_heads][splits][hd + 2]
-  int64_t visible;
+  float* scratch;  // [rows][n_heads][splits][hd + 2]
+  int64_t visible; // visible positions of query row 0 (row r sees visible + r)
   int n_heads;
   int n_kv_heads;
   int hd;
@@ -51,10 +51,12 @@ struct AttnArgs {
   float scale;
 };
 
-// Number of position slices for a launch: enough CTAs to cover every SM
-// twice, at least kMinSlice positions per slice.
-int Splits(int n_kv_heads, int64_t visible) {
-  const int64_t want = (2 * static_cast<int64_t>(SmCount()) + n_kv_heads - 1) / n_kv_heads;
+// Number of position slices for a launch of `rows` query rows: enough CTAs
+// to cover every SM twice, at least kMinSlice positions per slice (of the
+// longest row).
+int Splits(int n_kv_heads, int64_t visible, int64_t rows = 1) {
+  const int64_t ctas = static_cast<int64_t>(n_kv_heads) * rows;
+  const int64_t want = (2 * static_cast<int64_t>(SmCount()) + ctas - 1) / ctas;
   const int64_t most = (visible + kMinSlice - 1) / kMinSlice;
   int64_t s = want < most ? want : most;
   if (s < 1) s = 1;
@@ -70,9 +72,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
   const int warp = threadIdx.x >> 5;
   const int g = blockIdx.x;   // kv head
   const int s = blockIdx.y;   // slice
+  const int64_t row = blockIdx.z;
   const int hd4 = a.hd >> 2;
   const int64_t t_begin = s * a.slice;
-  const int64_t t_end = min(a.visible, t_begin + a.slice);
+  const int64_t t_end = min(a.visible + row, t_begin + a.slice);  // may be empty
+  const float* q_row = a.q + row * a.n_heads * a.hd;
+  float* scratch_row = a.scratch + row * a.n_heads * a.splits * (a.hd + 2);
   const int64_t stride4 = static_cast<int64_t>(a.n_kv_heads) * hd4;
 
   float4 q[G][NV];
@@ -81,7 +86,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const int i = lane + 32 * v;
-      q[h][v] = i < hd4 ? __ldg(reinterpret_cast<const float4*>(a.q) +
+      q[h][v] = i < hd4 ? __ldg(reinterpret_cast<const float4*>(q_row) +
                                 (static_cast<int64_t>(g) * G + h) * hd4 + i)
                         : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
       }
     }
     const int head = g * G + h;
-    float* part = a.scratch + (static_cast<int64_t>(head) * a.splits + s) * (a.hd + 2);
+    float* part = scratch_row + (static_cast<int64_t>(head) * a.splits + s) * (a.hd + 2);
     if (lane == 0) {
       part[0] = mm;
       part[1] = ll;
@@ -185,7 +190,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
 // out[h][i] = sum_s acc_s[i] * e^(m_s - M) / sum_s l_s * e^(m_s - M).
 __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
   const int head = blockIdx.x;
-  const float* base = a.scratch + static_cast<int64_t>(head) * a.splits * (a.hd + 2);
+  const int64_t row = blockIdx.y;
+  const float* base = a.scratch + (row * a.n_heads + head) * a.splits * (a.hd + 2);
   float mm = -INFINITY;
   for (int s = 0; s < a.splits; ++s) mm = fmaxf(mm, base[s * (a.hd + 2)]);
   float ll = 0.0f;
@@ -199,13 +205,14 @@ __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
       const float ms = base[s * (a.hd + 2)];
       if (ms != -INFINITY) sum = fmaf(base[s * (a.hd + 2) + 2 + i], expf(ms - mm), sum);
     }
-    a.out[static_cast<int64_t>(head) * a.hd + i] = __fdiv_rn(sum, ll);
+    a.out[(row * a.n_heads + head) * a.hd + i] = __fdiv_rn(sum, ll);
   }
 }
 
 template <int G>
-int LaunchPartial(const AttnArgs& a, int nv, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(a.n_kv_heads), static_cast<unsigned>(a.splits));
+int LaunchPartial(const AttnArgs& a, int64_t rows, int nv, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(a.n_kv_heads), static_cast<unsigned>(a.splits),
+                  static_cast<unsigned>(rows));
   if (nv == 1) {
     AttnPartialKernel<G, 1><<<grid, kAttnWarps * 32, 0, s>>>(a);
   } else {
@@ -244,46 +251,67 @@ int ValidateAttention(const float* q, const float* keys, const float* values,
 
 }  // namespace
 
-// Shared by the entry points: scratch must hold AttentionScratchFloats().
-int64_t AttentionScratchFloats(int n_heads, int n_kv_heads, int hd, int64_t visible) {
-  return static_cast<int64_t>(n_heads) * Splits(n_kv_heads, visible) * (hd + 2);
+// Shared by the entry points: scratch must hold AttentionScratchFloats() for
+// `rows` query rows, row r seeing visible + r positions.
+int64_t AttentionScratchFloats(int n_heads, int n_kv_heads, int hd, int64_t visible,
+                               int64_t rows) {
+  return rows * n_heads * Splits(n_kv_heads, visible + rows - 1, rows) * (hd + 2);
+}
+
+// Query rows [0, rows) at positions position + r (row r attends to cache
+// positions 0 .. position + r); q, out [rows, n_heads, hd].
+int AttentionRows(const float* q, const float* keys, const float* values, float* out,
+                  int64_t position, int64_t rows, int64_t max_seq, int n_heads,
+                  int n_kv_heads, int hd, float* scratch, void* stream) {
+  int rc = ValidateAttention(q, keys, values, out, position, max_seq, n_heads,
+                             n_kv_heads, hd);
+  if (rc != MLB_OK) return rc;
+  if (rows < 1 || position + rows > max_seq)
+    return Fail(MLB_ERR_RANGE, "attention: rows leave the cache");
+  AttnArgs a{};
+  a.keys = keys;
+  a.values = values;
+  a.scratch = scratch;
+  a.n_heads = n_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.hd = hd;
+  a.splits = Splits(n_kv_heads, position + rows, rows);
+  a.slice = (position + rows + a.splits - 1) / a.splits;
+  // 1 / std::sqrt((float)head_dim) as the reference computes it (forward.cc:75)
+  a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  const int nv = (hd / 4 + 31) / 32;
+  cudaStream_t s = AsStream(stream);
+  const int64_t per_row = static_cast<int64_t>(n_heads) * hd;
+  constexpr int64_t kMaxRowsPerLaunch = 65535;  // grid.z
+  for (int64_t r0 = 0; r0 < rows; r0 += kMaxRowsPerLaunch) {
+    const int64_t rc_rows = rows - r0 < kMaxRowsPerLaunch ? rows - r0 : kMaxRowsPerLaunch;
+    a.q = q + r0 * per_row;
+    a.out = out + r0 * per_row;
+    a.visible = position + r0 + 1;
+    switch (n_heads / n_kv_heads) {
+      case 1: rc = LaunchPartial<1>(a, rc_rows, nv, s); break;
+      case 2: rc = LaunchPartial<2>(a, rc_rows, nv, s); break;
+      case 3: rc = LaunchPartial<3>(a, rc_rows, nv, s); break;
+      case 4: rc = LaunchPartial<4>(a, rc_rows, nv, s); break;
+      case 5: rc = LaunchPartial<5>(a, rc_rows, nv, s); break;
+      case 6: rc = LaunchPartial<6>(a, rc_rows, nv, s); break;
+      case 7: rc = LaunchPartial<7>(a, rc_rows, nv, s); break;
+      case 8: rc = LaunchPartial<8>(a, rc_rows, nv, s); break;
+    }
+    if (rc != MLB_OK) return rc;
+    AttnCombineKernel<<<dim3(n_heads, static_cast<unsigned>(rc_rows)),
+                        hd < 256 ? ((hd + 31) / 32) * 32 : 256, 0, s>>>(a);
+    rc = CheckLaunch("attention");
+    if (rc != MLB_OK) return rc;
+  }
+  return MLB_OK;
 }
 
 int AttentionDecode(const float* q, const float* keys, const float* values,
                     float* out, int64_t position, int64_t max_seq, int n_heads,
                     int n_kv_heads, int hd, float* scratch, void* stream) {
-  int rc = ValidateAttention(q, keys, values, out, position, max_seq, n_heads,
-                             n_kv_heads, hd);
-  if (rc != MLB_OK) return rc;
-  AttnArgs a{};
-  a.q = q;
-  a.keys = keys;
-  a.values = values;
-  a.out = out;
-  a.scratch = scratch;
-  a.visible = position + 1;
-  a.n_heads = n_heads;
-  a.n_kv_heads = n_kv_heads;
-  a.hd = hd;
-  a.splits = Splits(n_kv_heads, a.visible);
-  a.slice = (a.visible + a.splits - 1) / a.splits;
-  // 1 / std::sqrt((float)head_dim) as the reference computes it (forward.cc:75)
-  a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
-  const int nv = (hd / 4 + 31) / 32;
-  cudaStream_t s = AsStream(stream);
-  switch (n_heads / n_kv_heads) {
-    case 1: rc = LaunchPartial<1>(a, nv, s); break;
-    case 2: rc = LaunchPartial<2>(a, nv, s); break;
-    case 3: rc = LaunchPartial<3>(a, nv, s); break;
-    case 4: rc = LaunchPartial<4>(a, nv, s); break;
-    case 5: rc = LaunchPartial<5>(a, nv, s); break;
-    case 6: rc = LaunchPartial<6>(a, nv, s); break;
-    case 7: rc = LaunchPartial<7>(a, nv, s); break;
-    case 8: rc = LaunchPartial<8>(a, nv, s); break;
-  }
-  if (rc != MLB_OK) return rc;
-  AttnCombineKernel<<<n_heads, hd < 256 ? ((hd + 31) / 32) * 32 : 256, 0, s>>>(a);
-  return CheckLaunch("mlb_attention_decode_f32");
+  return AttentionRows(q, keys, values, out, position, 1, max_seq, n_heads, n_kv_heads,
+                       hd, scratch, stream);
 }
 
 }  // namespace mlb
@@ -291,7 +319,7 @@ int AttentionDecode(const float* q, const float* keys, const float* values,
 extern "C" int64_t mlb_attention_scratch_floats(int n_heads, int n_kv_heads,
                                                 int head_dim, int64_t position) {
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || position < 0) return -1;
-  return mlb::AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1);
+  return mlb::AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1, 1);
 }
 
 extern "C" int mlb_attention_decode_f32(const float* q, const float* keys,
@@ -304,10 +332,34 @@ extern "C" int mlb_attention_decode_f32(const float* q, const float* keys,
   if (scratch == nullptr)
     return Fail(MLB_ERR_ARG, "mlb_attention_decode_f32: null scratch");
   if (n_heads > 0 && n_kv_heads > 0 && head_dim > 0 && position >= 0 &&
-      scratch_floats < AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1))
+      scratch_floats < AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1, 1))
     return Fail(MLB_ERR_ARG, "mlb_attention_decode_f32: scratch too small");
   return AttentionDecode(q, keys, values, out, position, max_seq, n_heads,
                          n_kv_heads, head_dim, scratch, stream);
+}
+
+extern "C" int64_t mlb_attention_rows_scratch_floats(int n_heads, int n_kv_heads,
+                                                     int head_dim, int64_t position,
+                                                     int64_t rows) {
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || position < 0 || rows < 1)
+    return -1;
+  return mlb::AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1, rows);
+}
+
+extern "C" int mlb_attention_rows_f32(const float* q, const float* keys,
+                                      const float* values, float* out, int64_t position,
+                                      int64_t rows, int64_t max_seq, int n_heads,
+                                      int n_kv_heads, int head_dim, float* scratch,
+                                      int64_t scratch_floats, void* stream) {
+  using namespace mlb;
+  if (rows == 0) return MLB_OK;
+  if (rows < 0) return Fail(MLB_ERR_ARG, "mlb_attention_rows_f32: rows < 0");
+  if (scratch == nullptr) return Fail(MLB_ERR_ARG, "mlb_attention_rows_f32: null scratch");
+  if (n_heads > 0 && n_kv_heads > 0 && head_dim > 0 && position >= 0 &&
+      scratch_floats < AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1, rows))
+    return Fail(MLB_ERR_ARG, "mlb_attention_rows_f32: scratch too small");
+  return AttentionRows(q, keys, values, out, position, rows, max_seq, n_heads, n_kv_heads,
+                       head_dim, scratch, stream);
 }
 
 extern "C" int mlb_kv_write_f32(float* keys, float* values, const float* k,
@@ -387,7 +439,7 @@ extern "C" int mlb_attention_decode_noalloc_f32(const float* q, const float* key
   using namespace mlb;
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || position < 0)
     return Fail(MLB_ERR_ARG, "mlb_attention_decode_noalloc_f32: bad sizes");
-  const int64_t need = AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1);
+  const int64_t need = AttentionScratchFloats(n_heads, n_kv_heads, head_dim, position + 1, 1);
   if (need > kNoAllocScratchFloats) {
     return Fail(MLB_ERR_ARG,
                 "mlb_attention_decode_noalloc_f32: these sizes need " +

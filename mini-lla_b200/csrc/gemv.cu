@@ -11,18 +11,20 @@
 // its F32 path calls cuBLAS SGEMV (:122-133).
 //
 // Design (memory-bound on W at T = 1):
-//   - streaming form (x of all tokens fits in 96 KB of shared memory):
-//     persistent CTAs of 8 warps copy x once; each warp streams its rows in
-//     1024-column segments through a 4-deep cp.async ring (no CTA barrier on
-//     the weight stream);
+//   - streaming form (x of all tokens fits in shared memory next to the
+//     weight rings; k % 128 == 0; 16-byte aligned table): persistent CTAs
+//     copy x once; each warp owns a contiguous run of rows and streams its
+//     weight blocks in ~2 KB segments, one bulk copy (cp.async.bulk +
+//     mbarrier) per segment, 3 segments ahead; products in packed fp32 pairs;
 //   - chunked form otherwise: one warp per output row, 8 rows per CTA;
-//   - the CTA walks k in chunks of kChunk = 1024 columns (32 blocks): all
+//     the CTA walks k in chunks of kChunk = 1024 columns (32 blocks): all
 //     threads copy x[:, chunk] for every token into shared memory (reused by
 //     the CTA's 8 rows), each warp copies its row's 32 blocks (the 16-byte
 //     aligned window) — both with cp.async, double-buffered so that chunk
-//     c + 1 is in flight while chunk c is computed — and lane l decodes the
-//     float4 groups l, l + 32, ... (8 lanes per block, conflict-free x reads);
-//   - block sums go to T fp32 accumulators per lane, reduced by shuffles.
+//     c + 1 is in flight while chunk c is computed;
+//   - in both, lane l decodes float4 group l % 8 of block l / 8 (8 lanes per
+//     block, conflict-free x reads) and block sums go to T fp32 accumulators
+//     per lane, reduced by shuffles.
 // HBM roofline per launch: n * row_bytes (weights) + 4 * T * (k + n).
 #include <climits>
 
@@ -213,121 +215,262 @@ __global__ void __launch_bounds__(256) GemvKernel(GemvArgs a, int slice) {
   }
 }
 
-// Streaming form, used when x for all T tokens fits in shared memory:
-// persistent CTAs copy x once; then every warp walks its rows segment by
-// segment (kChunk columns each) through a ring of kStages per-warp buffers
-// filled by cp.async kStages - 1 segments ahead.  No CTA-wide barrier sits
-// on the weight stream, so each warp keeps ~3 segments of weights in flight.
-constexpr int kStages = 4;
-constexpr int64_t kMaxResidentX = 96 * 1024;  // bytes of x kept in smem
-constexpr int64_t kMaxStreamSmem = 200 * 1024; // whole CTA (227 KB is the cap)
+// Packed fp32 pairs (sm_100 f32x2 instructions: two IEEE fp32 lanes per
+// instruction, each rounded like its scalar form).
+__device__ __forceinline__ uint64_t Pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float SumPair(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ uint64_t Add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t Mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t Fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// Four bytes -> two exact float pairs (the byte-permute conversion of
+// BytesToFloat4 with the bias subtracted two lanes at a time).
+__device__ __forceinline__ void BytesToPairs(uint32_t u, float bias, uint64_t& p01,
+                                             uint64_t& p23) {
+  const uint64_t nb = Pack2(-bias, -bias);
+  p01 = Add2(Pack2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                   __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), nb);
+  p23 = Add2(Pack2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                   __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), nb);
+}
+
+template <int QT>
+__device__ __forceinline__ void QuantPairs(const uint8_t* blk, int e, uint64_t& p01,
+                                           uint64_t& p23) {
+  if (QT == MLB_Q8_0) {
+    const uint32_t q = Smem16(blk + 2 + e) | (Smem16(blk + 4 + e) << 16);
+    BytesToPairs(q ^ 0x80808080u, 8388736.0f, p01, p23);
+    return;
+  }
+  uint32_t q;
+  if (QT == MLB_Q4_0) {
+    q = Smem16(blk + 2 + (e & 15)) | (Smem16(blk + 4 + (e & 15)) << 16);
+  } else {
+    q = *reinterpret_cast<const uint32_t*>(blk + 4 + (e & 15));
+  }
+  if (e >= 16) q >>= 4;
+  BytesToPairs(q & 0x0F0F0F0Fu, QT == MLB_Q4_0 ? 8388616.0f : 8388608.0f, p01, p23);
+}
+
+// mbarrier + bulk-copy helpers (one elected lane issues, the warp waits).
+__device__ __forceinline__ unsigned SmemAddr(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void BarInit(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(SmemAddr(bar)),
+               "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void BarExpectTx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(
+                   SmemAddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// One poll suspends the thread for at most ~kSuspendNs (it resumes as soon
+// as the phase completes).
+constexpr int kSuspendNs = 1000;
+__device__ __forceinline__ bool BarTryWait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(SmemAddr(bar)), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after kWaitLimit polls, ~2 s (a copy that never
+// lands must not hang the device).
+constexpr int kWaitLimit = 1 << 21;
+__device__ __forceinline__ bool BarWait(uint64_t* bar, unsigned parity) {
+  for (int i = 0; i < kWaitLimit; ++i)
+    if (BarTryWait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void BulkCopy(void* dst, const void* src, unsigned bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1], %2, [%3];\n" ::"r"(SmemAddr(dst)),
+      "l"(src), "r"(bytes), "r"(SmemAddr(bar))
+      : "memory");
+}
+
+}  // namespace
+
+// Waits that gave up (a bulk copy that did not land in time); read by
+// mlb_wait_timeouts.
+__device__ unsigned int g_wait_timeouts;
+
+namespace {
+
+// Streaming form, used when x for all T tokens fits in shared memory next
+// to the weight rings.  Persistent CTAs copy x once; the rows are split
+// evenly over CTAs and then over each CTA's warps, so a warp owns a
+// contiguous run of rows = a contiguous run of weight blocks.  The warp
+// streams that run in segments of `sb` blocks (a multiple of 8, so every
+// segment starts 16-byte aligned: 8 blocks are 272 / 144 / 160 bytes)
+// through a ring of kBulkStages slots: lane 0 issues one bulk copy per
+// segment (cp.async.bulk, completion on the slot's mbarrier) kBulkStages - 1
+// segments ahead.  Lane l decodes float4 group l % 8 of block l / 8 of each
+// group of 4 blocks (conflict-free x reads; the row length in blocks is a
+// multiple of 4, so a group never straddles two rows) and accumulates in
+// packed fp32 pairs.
+constexpr int kBulkStages = 4;
+constexpr int kBulkMaxWarps = 16;
+constexpr int kBarBytes = kBulkMaxWarps * kBulkStages * 8;
+constexpr int64_t kMaxBulkSmem = 220 * 1024;
+
+template <int QT>
+__host__ __device__ constexpr int BlockBytes() {  // bytes per 32 columns
+  return QT == MLB_F32 ? 128 : (QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20));
+}
 
 template <int QT, int T>
-__global__ void __launch_bounds__(256) GemvStreamKernel(GemvArgs a, int slice,
-                                                        int rows_per_warp) {
+__global__ void __launch_bounds__(kBulkMaxWarps * 32)
+    GemvBulkKernel(GemvArgs a, int sb, int slot_bytes) {
   extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
+  constexpr int kBB = BlockBytes<QT>();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
   const int k4 = a.k >> 2;
-  float4* xs = reinterpret_cast<float4*>(smem);
-  uint8_t* ring = smem + static_cast<size_t>(T) * a.k * 4 +
-                  static_cast<size_t>(warp) * kStages * slice;
-  // x for every token, once per CTA
-  const float4* x4 = reinterpret_cast<const float4*>(a.x);
-  for (int i = threadIdx.x; i < T * k4; i += blockDim.x) CopyAsync16(xs + i, x4 + i);
-  CopyAsyncCommit();
+  const int nb = a.k >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kBulkStages;
+  const float4* xs = reinterpret_cast<const float4*>(smem + kBarBytes);
+  uint8_t* ring = smem + kBarBytes + static_cast<size_t>(T) * a.k * 4 +
+                  static_cast<size_t>(warp) * kBulkStages * slot_bytes;
+
+  {  // x for every token, once per CTA
+    float4* xd = reinterpret_cast<float4*>(smem + kBarBytes);
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    for (int i = threadIdx.x; i < T * k4; i += blockDim.x) CopyAsync16(xd + i, x4 + i);
+    CopyAsyncCommit();
+  }
+  if (lane == 0) {
+    for (int s = 0; s < kBulkStages; ++s) BarInit(bars + s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   CopyAsyncWait<0>();
   __syncthreads();
 
-  const int nseg = (a.k + kChunk - 1) / kChunk;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + warp) *
-                       rows_per_warp;
-  int64_t rows = a.n - row0;
-  if (rows > rows_per_warp) rows = rows_per_warp;
-  const int items = rows > 0 ? static_cast<int>(rows) * nseg : 0;
+  const int64_t c0 = a.n * blockIdx.x / gridDim.x;
+  const int64_t c1 = a.n * (blockIdx.x + 1) / gridDim.x;
+  const int64_t w0 = c0 + (c1 - c0) * warp / warps;
+  const int64_t w1 = c0 + (c1 - c0) * (warp + 1) / warps;
+  if (w0 >= w1) return;
+  const int64_t first = w0 * nb;               // this warp's first block
+  const int64_t b0 = first & ~int64_t{7};      // segment grid start (aligned)
+  const int64_t b1 = w1 * nb;
+  const int nseg = static_cast<int>((b1 - b0 + sb - 1) / sb);
 
-  // byte offset of item i's segment in the weight table
-  auto seg_start = [&](int i) -> int64_t {
-    const int64_t j = row0 + i / nseg;
-    const int sg = i % nseg;
-    return j * a.row_bytes + (QT == MLB_F32 ? static_cast<int64_t>(sg) * kChunk * 4
-                                            : static_cast<int64_t>(sg) * 32 * kBB);
-  };
-  auto seg_bytes = [&](int i) -> int64_t {
-    const int cols = min(kChunk, a.k - (i % nseg) * kChunk);
-    return QT == MLB_F32 ? static_cast<int64_t>(cols) * 4
-                         : static_cast<int64_t>(cols / 32) * kBB;
-  };
-  auto issue = [&](int i) {
-    uint8_t* dst = ring + (i % kStages) * slice;
-    const int64_t start = seg_start(i);
-    const int64_t window = start & ~int64_t{15};
-    const int n16 = static_cast<int>((start + seg_bytes(i) - window + 15) >> 4);
-    for (int q = lane; q < n16; q += 32) {
-      const int64_t off = window + 16 * static_cast<int64_t>(q);
-      if (off + 16 <= a.table_bytes) {
-        CopyAsync16(dst + 16 * q, a.w + off);
-      } else {
-        for (int b = 0; b < 16; ++b)
-          dst[16 * q + b] = off + b < a.table_bytes ? a.w[off + b] : 0;
-      }
+  auto issue = [&](int s) {
+    if (lane != 0) return;
+    const int64_t gb = b0 + static_cast<int64_t>(s) * sb;
+    const int64_t ge = gb + sb < b1 ? gb + sb : b1;
+    const int64_t start = gb * kBB;
+    const int64_t bytes = (ge - gb) * kBB;
+    int64_t copy = (bytes + 15) & ~int64_t{15};
+    const int64_t room = (a.table_bytes - start) & ~int64_t{15};
+    if (copy > room) copy = room;  // the table's last < 16 bytes: plain loads
+    uint8_t* dst = ring + (s % kBulkStages) * slot_bytes;
+    uint64_t* bar = bars + s % kBulkStages;
+    if (copy < bytes) {
+      for (int64_t b = copy; b < bytes; ++b) dst[b] = a.w[start + b];
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
+    BarExpectTx(bar, static_cast<unsigned>(copy));
+    if (copy > 0) BulkCopy(dst, a.w + start, static_cast<unsigned>(copy), bar);
   };
 
-  for (int i = 0; i < kStages - 1; ++i) {
-    if (i < items) issue(i);
-    CopyAsyncCommit();
-  }
-  float acc[T];
+  for (int s = 0; s < kBulkStages - 1 && s < nseg; ++s) issue(s);
+  uint64_t acc[T];
 #pragma unroll
-  for (int t = 0; t < T; ++t) acc[t] = 0.0f;
-  for (int i = 0; i < items; ++i) {
-    if (i + kStages - 1 < items) issue(i + kStages - 1);
-    CopyAsyncCommit();
-    CopyAsyncWait<kStages - 1>();  // item i's copies (this lane's) landed
-    __syncwarp();                  // ... and every lane's
-    const int sg = i % nseg;
-    const int c4 = min(kChunk, a.k - sg * kChunk) >> 2;
-    const int64_t start = seg_start(i);
-    const uint8_t* seg = ring + (i % kStages) * slice + (start & 15);
-    const float4* xseg = xs + sg * (kChunk / 4);
-    if (QT == MLB_F32) {
-      const float4* w4 = reinterpret_cast<const float4*>(seg);
-      for (int o = lane; o < c4; o += 32) {
-        const float4 w = w4[o];
-#pragma unroll
-        for (int t = 0; t < T; ++t) acc[t] = Dot4(w, xseg[t * k4 + o], acc[t]);
-      }
-    } else {
-      for (int o = lane; o < c4; o += 32) {
-        const uint8_t* blk = seg + (o >> 3) * kBB;
-        const float4 q = QuantValues<QT>(blk, (o & 7) * 4);
-        const uint32_t scale = QT == MLB_Q4_1
-                                   ? *reinterpret_cast<const uint32_t*>(blk)
-                                   : Smem16(blk);
-        const float d = HalfBits(scale & 0xffffu);
-        const float m = QT == MLB_Q4_1 ? HalfBits(scale >> 16) : 0.0f;
+  for (int t = 0; t < T; ++t) acc[t] = 0;  // (+0.0f, +0.0f)
+  int64_t row = w0;
+  int kb = 0;  // block index of the current group inside `row`
+  for (int s = 0; s < nseg; ++s) {
+    if (s + kBulkStages - 1 < nseg) issue(s + kBulkStages - 1);
+    if (!BarWait(bars + s % kBulkStages, (s / kBulkStages) & 1)) {
+      // give up: count it, let the copies in flight land (bounded), and
+      // leave NaN in the rows this warp did not finish
+      if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
+      const int last = s + kBulkStages - 1 < nseg ? s + kBulkStages - 1 : nseg - 1;
+      for (int r = s; r <= last; ++r) BarWait(bars + r % kBulkStages, (r / kBulkStages) & 1);
+      for (int64_t j = row; j < w1; ++j)
+        if (lane < T) a.y[static_cast<int64_t>(lane) * a.n + j] = __int_as_float(0x7fc00000);
+      return;
+    }
+    const int64_t gb = b0 + static_cast<int64_t>(s) * sb;
+    const int count = static_cast<int>((gb + sb < b1 ? gb + sb : b1) - gb);
+    const uint8_t* slot = ring + (s % kBulkStages) * slot_bytes;
+    for (int b = s == 0 ? static_cast<int>(first - b0) : 0; b < count; b += 4) {
+      const uint8_t* blk = slot + (b + (lane >> 3)) * kBB;
+      const int xo = kb * 8 + lane;  // this lane's x float4
+      if (QT == MLB_F32) {
+        const float4 w = *reinterpret_cast<const float4*>(blk + (lane & 7) * 16);
+        const uint64_t w01 = Pack2(w.x, w.y), w23 = Pack2(w.z, w.w);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-          const float4 xv = xseg[t * k4 + o];
-          acc[t] = fmaf(d, Dot4(q, xv, 0.0f), acc[t]);
-          if (QT == MLB_Q4_1) acc[t] = fmaf(m, (xv.x + xv.y) + (xv.z + xv.w), acc[t]);
+          const float4 xv = xs[t * k4 + xo];
+          acc[t] = Fma2(w01, Pack2(xv.x, xv.y), acc[t]);
+          acc[t] = Fma2(w23, Pack2(xv.z, xv.w), acc[t]);
+        }
+      } else {
+        uint64_t q01, q23;
+        QuantPairs<QT>(blk, (lane & 7) * 4, q01, q23);
+        const uint32_t scale = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(blk)
+                                              : Smem16(blk);
+        const float d = HalfBits(scale & 0xffffu);
+        const uint64_t d2 = Pack2(d, d);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 xv = xs[t * k4 + xo];
+          const uint64_t x01 = Pack2(xv.x, xv.y), x23 = Pack2(xv.z, xv.w);
+          const uint64_t p = Fma2(q23, x23, Mul2(q01, x01));
+          acc[t] = Fma2(d2, p, acc[t]);
+          if (QT == MLB_Q4_1) {
+            const float m = HalfBits(scale >> 16);
+            acc[t] = Fma2(Pack2(m, m), Add2(x01, x23), acc[t]);
+          }
         }
       }
-    }
-    if (sg == nseg - 1) {
-      const int64_t j = row0 + i / nseg;
+      kb += 4;
+      if (kb == nb) {
 #pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const float sum = WarpSum(acc[t]);
-        if (lane == t) a.y[static_cast<int64_t>(t) * a.n + j] = sum;
-        acc[t] = 0.0f;
+        for (int t = 0; t < T; ++t) {
+          const float sum = WarpSum(SumPair(acc[t]));
+          if (lane == t) a.y[static_cast<int64_t>(t) * a.n + row] = sum;
+          acc[t] = 0;
+        }
+        ++row;
+        kb = 0;
       }
     }
-    __syncwarp();  // the slot is read by every lane before it is refilled
+    __syncwarp();  // the slot is read by every lane before lane 0 refills it
   }
-  CopyAsyncWait<0>();
 }
 
 // Any k / alignment: one thread per output element, the reference's
@@ -378,48 +521,50 @@ bool AllowSmem(K kernel, size_t bytes) {
 }
 
 template <int QT, int T>
-int LaunchStream(const GemvArgs& a, cudaStream_t s) {
-  constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
-  const int seg = QT == MLB_F32 ? kChunk * 4 : 32 * kBB;
-  const int slice = (seg + 15 + 15) / 16 * 16;
-  const size_t shm = static_cast<size_t>(T) * a.k * 4 +
-                     static_cast<size_t>(kWarpsPerCta) * kStages * slice;
-  auto kernel = GemvStreamKernel<QT, T>;
+int LaunchBulk(const GemvArgs& a, int warps, int sb, int slot, cudaStream_t s) {
+  const size_t shm = kBarBytes + static_cast<size_t>(T) * a.k * 4 +
+                     static_cast<size_t>(warps) * kBulkStages * slot;
+  auto kernel = GemvBulkKernel<QT, T>;
   if (!AllowSmem(kernel, shm))
     return Fail(MLB_ERR_CUDA, "mlb_linear_f32: shared memory opt-in");
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, shm) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, warps * 32, shm) !=
           cudaSuccess ||
       per_sm < 1) {
     cudaGetLastError();
     per_sm = 1;
   }
-  // spread rows evenly: every warp gets rows_per_warp consecutive rows
-  const int64_t max_warps = static_cast<int64_t>(per_sm) * SmCount() * kWarpsPerCta;
-  const int64_t rows_per_warp = (a.n + max_warps - 1) / max_warps;
-  const int64_t warps = (a.n + rows_per_warp - 1) / rows_per_warp;
-  const int64_t blocks = (warps + kWarpsPerCta - 1) / kWarpsPerCta;
-  kernel<<<static_cast<unsigned>(blocks), 256, shm, s>>>(a, slice,
-                                                        static_cast<int>(rows_per_warp));
+  int64_t blocks = static_cast<int64_t>(per_sm) * SmCount();
+  const int64_t needed = (a.n + warps - 1) / warps;  // at least a row per warp
+  if (blocks > needed) blocks = needed;
+  kernel<<<static_cast<unsigned>(blocks), warps * 32, shm, s>>>(a, sb, slot);
   return CheckLaunch("mlb_linear_f32");
 }
 
 template <int QT>
-int LaunchVec(const GemvArgs& a, int t_rows, cudaStream_t s) {
-  constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
-  const int64_t ring = static_cast<int64_t>(kWarpsPerCta) * kStages *
-                       (((QT == MLB_F32 ? kChunk * 4 : 32 * kBB) + 30) / 16 * 16);
+int LaunchVec(const GemvArgs& a, int t_rows, bool bulk_ok, cudaStream_t s) {
+  constexpr int kBB = BlockBytes<QT>();
+  // segments of ~2 KB: 16 F32 blocks, 64 Q8_0 blocks, 128 Q4 blocks
+  const int sb = QT == MLB_F32 ? 16 : (QT == MLB_Q8_0 ? 64 : 128);
+  const int slot = (sb * kBB + 15) / 16 * 16;
   const int64_t x_bytes = static_cast<int64_t>(t_rows) * a.k * 4;
-  if (x_bytes <= kMaxResidentX && x_bytes + ring <= kMaxStreamSmem) {
+  // warps per CTA: enough CTAs to spread few rows over the SMs, at most 16,
+  // at least 4, and all rings plus x inside the shared-memory budget
+  int warps = static_cast<int>((a.n + SmCount() - 1) / SmCount());
+  warps = warps < 4 ? 4 : (warps > kBulkMaxWarps ? kBulkMaxWarps : warps);
+  while (warps > 4 && kBarBytes + x_bytes + int64_t{warps} * kBulkStages * slot > kMaxBulkSmem)
+    --warps;
+  if (bulk_ok && (a.k % 128) == 0 &&
+      kBarBytes + x_bytes + int64_t{warps} * kBulkStages * slot <= kMaxBulkSmem) {
     switch (t_rows) {
-      case 1: return LaunchStream<QT, 1>(a, s);
-      case 2: return LaunchStream<QT, 2>(a, s);
-      case 3: return LaunchStream<QT, 3>(a, s);
-      case 4: return LaunchStream<QT, 4>(a, s);
-      case 5: return LaunchStream<QT, 5>(a, s);
-      case 6: return LaunchStream<QT, 6>(a, s);
-      case 7: return LaunchStream<QT, 7>(a, s);
-      case 8: return LaunchStream<QT, 8>(a, s);
+      case 1: return LaunchBulk<QT, 1>(a, warps, sb, slot, s);
+      case 2: return LaunchBulk<QT, 2>(a, warps, sb, slot, s);
+      case 3: return LaunchBulk<QT, 3>(a, warps, sb, slot, s);
+      case 4: return LaunchBulk<QT, 4>(a, warps, sb, slot, s);
+      case 5: return LaunchBulk<QT, 5>(a, warps, sb, slot, s);
+      case 6: return LaunchBulk<QT, 6>(a, warps, sb, slot, s);
+      case 7: return LaunchBulk<QT, 7>(a, warps, sb, slot, s);
+      case 8: return LaunchBulk<QT, 8>(a, warps, sb, slot, s);
     }
   }
   const int slice = QT == MLB_F32 ? 0 : (32 * kBB + 15 + 15) / 16 * 16;
@@ -442,6 +587,14 @@ int LaunchVec(const GemvArgs& a, int t_rows, cudaStream_t s) {
 
 }  // namespace
 }  // namespace mlb
+
+extern "C" int mlb_wait_timeouts(unsigned int* count) {
+  using namespace mlb;
+  if (count == nullptr) return Fail(MLB_ERR_ARG, "mlb_wait_timeouts: null pointer");
+  if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
+    return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
+  return MLB_OK;
+}
 
 extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                               const float* x, int64_t t_rows, float* y,
@@ -470,6 +623,9 @@ extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                        256, 0, s>>>(a, qtype, t_rows);
     return CheckLaunch("mlb_linear_f32");
   }
+  // bulk copies need a 16-byte aligned table (segments start on 8-block,
+  // i.e. 16-byte, boundaries of it)
+  const bool bulk_ok = (wp & 15u) == 0;
   // token groups of up to kMaxTokens reuse each staged weight chunk
   for (int64_t t0 = 0; t0 < t_rows; t0 += kMaxTokens) {
     const int tg = static_cast<int>(t_rows - t0 < kMaxTokens ? t_rows - t0 : kMaxTokens);
@@ -477,10 +633,10 @@ extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                n * row_bytes, x + t0 * k, y + t0 * n};
     int rc = MLB_OK;
     switch (qtype) {
-      case MLB_F32: rc = LaunchVec<MLB_F32>(a, tg, s); break;
-      case MLB_Q8_0: rc = LaunchVec<MLB_Q8_0>(a, tg, s); break;
-      case MLB_Q4_0: rc = LaunchVec<MLB_Q4_0>(a, tg, s); break;
-      case MLB_Q4_1: rc = LaunchVec<MLB_Q4_1>(a, tg, s); break;
+      case MLB_F32: rc = LaunchVec<MLB_F32>(a, tg, bulk_ok, s); break;
+      case MLB_Q8_0: rc = LaunchVec<MLB_Q8_0>(a, tg, bulk_ok, s); break;
+      case MLB_Q4_0: rc = LaunchVec<MLB_Q4_0>(a, tg, bulk_ok, s); break;
+      case MLB_Q4_1: rc = LaunchVec<MLB_Q4_1>(a, tg, bulk_ok, s); break;
     }
     if (rc != MLB_OK) return rc;
   }

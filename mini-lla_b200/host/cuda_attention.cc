@@ -12,6 +12,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "mini_llama/cuda_layer_ops.h"
 #include "mlb_ops.h"
 
 namespace mini_lla {
@@ -104,6 +105,49 @@ CudaTensor CudaAttention(const CudaTensor& q, const CudaKvCache& cache,
                                  n_kv_heads, head_dim,
                                  static_cast<float*>(scratch.data()), need, nullptr),
         "CudaAttention");
+  return output;
+}
+
+void CudaKvCacheWriteRows(CudaKvCache* cache, int layer, int position,
+                          const CudaTensor& keys, const CudaTensor& values) {
+  if (cache == nullptr) throw std::invalid_argument("CudaKvCacheWriteRows: null cache");
+  CheckCache(*cache, layer, position);
+  const size_t per = static_cast<size_t>(cache->kv_heads()) * cache->head_dim();
+  if (keys.Size() != values.Size() || keys.Size() % per != 0) {
+    throw std::invalid_argument("CudaKvCacheWriteRows: tensor shape mismatch");
+  }
+  const int64_t rows = static_cast<int64_t>(keys.Size() / per);
+  // the cache's layer buffers are device memory it owns; Keys()/Values() hand
+  // them out read-only, the write goes through the same addresses
+  float* k_layer = const_cast<float*>(cache->Keys(layer));
+  float* v_layer = const_cast<float*>(cache->Values(layer));
+  Check(mlb_kv_write_f32(k_layer, v_layer, keys.data(), values.data(), position, rows,
+                         cache->max_seq(), cache->kv_heads(), cache->head_dim(), nullptr),
+        "CudaKvCacheWriteRows");
+}
+
+CudaTensor CudaAttentionRows(const CudaTensor& q, const CudaKvCache& cache,
+                             int layer, int position, int n_heads,
+                             int n_kv_heads, int head_dim) {
+  CheckCache(cache, layer, position);
+  const size_t per = static_cast<size_t>(n_heads) * head_dim;
+  if (per == 0 || q.Size() % per != 0 || n_kv_heads != cache.kv_heads() ||
+      head_dim != cache.head_dim()) {
+    throw std::invalid_argument("CudaAttentionRows: shape mismatch");
+  }
+  const int rows = static_cast<int>(q.Size() / per);
+  CudaTensor output({rows, n_heads * head_dim});
+  if (rows == 0) return output;
+  const int64_t need = mlb_attention_rows_scratch_floats(n_heads, n_kv_heads, head_dim,
+                                                         position, rows);
+  if (need < 0) throw std::invalid_argument("CudaAttentionRows: bad sizes");
+  DeviceBuffer scratch;  // pooled; reuse is ordered on the default stream
+  scratch.Reset(static_cast<size_t>(need) * sizeof(float));
+  Check(mlb_attention_rows_f32(q.data(), cache.Keys(layer), cache.Values(layer),
+                               output.data(), position, rows, cache.max_seq(), n_heads,
+                               n_kv_heads, head_dim, static_cast<float*>(scratch.data()),
+                               need, nullptr),
+        "CudaAttentionRows");
   return output;
 }
 

@@ -6,32 +6,56 @@
 // thread per output row.
 #include "mini_llama/cuda_matmul.h"
 
+#include <cstdint>
 #include <stdexcept>
 #include <string>
 
+#include "mini_llama/cuda_layer_ops.h"
 #include "mlb_ops.h"
 
 namespace mini_lla {
+
+namespace {
+
+int QType(QuantType type) {
+  switch (type) {
+    case QuantType::kF32: return MLB_F32;
+    case QuantType::kQ8_0: return MLB_Q8_0;
+    case QuantType::kQ4_0: return MLB_Q4_0;
+    case QuantType::kQ4_1: return MLB_Q4_1;
+  }
+  throw std::invalid_argument("unknown quant type");
+}
+
+void Linear(const CudaTensor& x, const CudaWeight& weight, int64_t rows,
+            CudaTensor* output, const char* caller) {
+  const int rc = mlb_linear_f32(weight.buffer.data(), QType(weight.type), weight.rows,
+                                weight.cols, x.data(), rows, output->data(), nullptr);
+  if (rc != MLB_OK) {
+    const std::string message = std::string(caller) + ": " + mlb_last_error();
+    if (rc == MLB_ERR_ARG) throw std::invalid_argument(message);
+    throw std::runtime_error(message);
+  }
+}
+
+}  // namespace
 
 CudaTensor CudaLinear(const CudaTensor& x, const CudaWeight& weight) {
   if (x.Size() != static_cast<size_t>(weight.cols)) {
     throw std::invalid_argument("CudaLinear: input size mismatch");
   }
   CudaTensor output({weight.rows});
-  int qtype = MLB_F32;
-  switch (weight.type) {
-    case QuantType::kF32: qtype = MLB_F32; break;
-    case QuantType::kQ8_0: qtype = MLB_Q8_0; break;
-    case QuantType::kQ4_0: qtype = MLB_Q4_0; break;
-    case QuantType::kQ4_1: qtype = MLB_Q4_1; break;
+  Linear(x, weight, 1, &output, "CudaLinear");
+  return output;
+}
+
+CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight) {
+  if (weight.cols <= 0 || x.shape().empty() || x.shape().back() != weight.cols) {
+    throw std::invalid_argument("CudaLinearRows: input size mismatch");
   }
-  const int rc = mlb_linear_f32(weight.buffer.data(), qtype, weight.rows,
-                                weight.cols, x.data(), 1, output.data(), nullptr);
-  if (rc != MLB_OK) {
-    const std::string message = std::string("CudaLinear: ") + mlb_last_error();
-    if (rc == MLB_ERR_ARG) throw std::invalid_argument(message);
-    throw std::runtime_error(message);
-  }
+  const int rows = static_cast<int>(x.Size() / static_cast<size_t>(weight.cols));
+  CudaTensor output({rows, weight.rows});
+  if (rows > 0) Linear(x, weight, rows, &output, "CudaLinearRows");
   return output;
 }
 

@@ -262,6 +262,23 @@ CudaTensor CudaAddRmsNormRows(const CudaTensor& x, const CudaTensor* residual,
   return output;
 }
 
+CudaTensor CudaAddBiasRows(const CudaTensor& value, const CudaWeight* bias) {
+  if (value.shape().empty()) {
+    throw std::invalid_argument("CudaAddBiasRows: expected rows");
+  }
+  const int64_t cols = value.shape().back();
+  if (bias != nullptr && WeightSize(*bias) != static_cast<size_t>(cols)) {
+    throw std::invalid_argument("CudaAddBiasRows: bias size mismatch");
+  }
+  CudaTensor output(value.shape());
+  if (value.Size() == 0) return output;
+  Check(mlb_add_bias_f32(value.data(), bias == nullptr ? nullptr : F32(*bias),
+                         output.data(), static_cast<int64_t>(value.Size()) / cols, cols,
+                         nullptr),
+        "CudaAddBiasRows");
+  return output;
+}
+
 CudaTensor CudaSwiGlu(const CudaTensor& gate, const CudaTensor& up) {
   if (gate.shape() != up.shape()) {
     throw std::invalid_argument("CudaSwiGlu: shape mismatch");

@@ -16,6 +16,7 @@
 #include <utility>
 #include <vector>
 
+#include "mini_llama/cuda_attention.h"
 #include "mini_llama/cuda_tensor.h"
 #include "mini_llama/cuda_weights.h"
 #include "mini_llama/ops.h"
@@ -51,6 +52,29 @@ CudaTensor CudaSoftmaxRows(const CudaTensor& x,
 // One dequantised embedding row per token id -> [tokens.size(), cols].
 CudaTensor CudaEmbeddingRows(const CudaWeight& embedding,
                              const std::vector<int>& tokens);
+
+// y[r] = W . x[r] for every row of x [rows, weight.cols] -> [rows,
+// weight.rows] (CudaLinear, cuda_matmul.h, for a batch of tokens).
+CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight);
+
+// value[r] + bias for every row of value [rows, bias size] (AddBias,
+// forward.cc:36-47, for a batch of tokens); a null bias copies value.
+CudaTensor CudaAddBiasRows(const CudaTensor& value, const CudaWeight* bias);
+
+// Writes the K/V of rows consecutive tokens (keys, values [rows, kv_heads *
+// head_dim]) to positions [position, position + rows) of `layer`
+// (CudaKvCache::Write for a batch of tokens).  std::out_of_range when the
+// positions or the layer leave the cache.
+void CudaKvCacheWriteRows(CudaKvCache* cache, int layer, int position,
+                          const CudaTensor& keys, const CudaTensor& values);
+
+// Causal attention of q [rows, n_heads * head_dim] whose row r is the token
+// at position + r, over `layer` of the cache (its K/V must be written for
+// every position up to position + rows - 1) -> [rows, n_heads * head_dim];
+// row r equals CudaAttention at position + r.
+CudaTensor CudaAttentionRows(const CudaTensor& q, const CudaKvCache& cache,
+                             int layer, int position, int n_heads,
+                             int n_kv_heads, int head_dim);
 
 // Makes `device` current for the scope and restores the previous device.
 class CudaDeviceScope {

@@ -50,6 +50,12 @@ SIGNATURES = {
                                      c_void_p, c_int64, c_void_p, c_void_p,
                                      c_void_p]),
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "mlb_wait_timeouts": (c_int, [c_void_p]),
+    "mlb_attention_rows_scratch_floats": (c_int64, [c_int, c_int, c_int, c_int64,
+                                                    c_int64]),
+    "mlb_attention_rows_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_int64, c_int64, c_int64, c_int, c_int,
+                                       c_int, c_void_p, c_int64, c_void_p]),
     "mlb_linear_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                c_int64, c_void_p, c_void_p]),
     "mlb_kv_write_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
@@ -372,6 +378,29 @@ def attention_decode(q, keys, values, position: int, out=None, scratch=None,
     return out
 
 
+def attention_rows(q, keys, values, position: int, out=None, scratch=None,
+                   stream=None):
+    """Causal attention of q [rows, n_heads, hd] (row r at position + r) over
+    one layer's cache [max_seq, kv_heads, hd] -> [rows, n_heads, hd]."""
+    import torch
+    op = "attention_rows"
+    for t, name in ((q, "q"), (keys, "keys"), (values, "values")):
+        _f32_cuda(t, op, name)
+    max_seq, kvh, hd = keys.shape
+    rows, nh = q.shape[0], q.shape[1]
+    if out is None:
+        out = torch.empty((rows, nh, hd), dtype=torch.float32, device=q.device)
+    if rows == 0:
+        return out
+    need = load().mlb_attention_rows_scratch_floats(nh, kvh, hd, int(position), rows)
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.float32, device=q.device)
+    _check(load().mlb_attention_rows_f32(
+        _ptr(q), _ptr(keys), _ptr(values), _ptr(out), int(position), rows, max_seq,
+        nh, kvh, hd, _ptr(scratch), scratch.numel(), _stream(stream)), op)
+    return out
+
+
 def status_check(status, stream=None) -> int:
     """Synchronises and returns the device status bits (0 = clean)."""
     bits = ctypes.c_int32(0)
@@ -380,3 +409,11 @@ def status_check(status, stream=None) -> int:
     if rc not in (0, 3):
         _check(rc, "status_check")
     return bits.value
+
+
+def wait_timeouts() -> int:
+    """Bounded device waits that gave up on the current device (0 when every
+    bulk copy landed in time)."""
+    count = ctypes.c_uint(0)
+    _check(load().mlb_wait_timeouts(ctypes.byref(count)), "wait_timeouts")
+    return count.value

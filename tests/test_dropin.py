@@ -63,3 +63,21 @@ def test_reference_api_dropin_binary():
     res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "dropin ok" in res.stdout
+
+
+@pytest.mark.gpu
+def test_prefill_driver_and_weight_upload_binary():
+    """oracle/_ref/mlb_forward_test: ForwardBatchCuda (row-batched prefill)
+    and the device weight / GGUF upload paths against the reference's CPU
+    ForwardBatch and its per-token GPU driver on random models (Q8_0, Q4_0,
+    Q4_1, F32; GQA, biases, NeoX, tied output) and on the reference's GGUF
+    test fixture; logits within 2e-5 of the largest logit."""
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    exe = os.path.join(REF, "mlb_forward_test")
+    if not os.path.exists(exe):
+        pytest.skip("mlb_forward_test not built (reference headers absent)")
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "forward ok" in res.stdout

@@ -100,3 +100,39 @@ def test_kv_write_is_a_copy(cuda):
     assert not kh[:7].any() and not kh[8:45].any()
     with pytest.raises(IndexError):
         mlb.kv_write(keys, values, dev(kb, cuda), dev(vb, cuda), 46)
+
+
+@pytest.mark.parametrize("nh,nkv,hd,pos,rows,max_seq", [
+    (4, 2, 8, 0, 1, 16), (8, 2, 64, 0, 37, 64), (32, 8, 128, 100, 64, 512),
+    (14, 2, 64, 0, 256, 256), (28, 4, 128, 2000, 48, 4096), (8, 8, 32, 5, 300, 400)])
+def test_attention_rows_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max_seq):
+    """Row r of a prompt chunk equals decode attention at position pos + r
+    (the reference's per-token loop, batch.cc:26-41 over forward.cc:50-95)."""
+    import torch
+    rng = np.random.default_rng(nh * 7 + rows)
+    q = rng.standard_normal((rows, nh, hd), dtype=np.float32)
+    keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    values = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    got = mlb.attention_rows(dev(q, cuda), dev(keys, cuda), dev(values, cuda), pos)
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    for r in sorted({0, rows // 3, rows // 2, rows - 1}):
+        want = oracle.attention_decode(q[r], keys, values, pos + r, nh, nkv)
+        mag = _magnitude(q[r], keys, values, pos + r, nh, nkv)
+        err = np.abs(got[r].astype(np.float64) - want)
+        ratio = float((err / np.maximum(mag, 1e-30)).max())
+        assert ratio <= 1e-5, f"row {r}: max error / magnitude {ratio:.2e}"
+
+
+def test_attention_rows_rejects_rows_beyond_cache(cuda):
+    nh, nkv, hd, max_seq = 4, 2, 16, 32
+    keys = torch_zeros((max_seq, nkv, hd), cuda)
+    with pytest.raises(IndexError):
+        mlb.attention_rows(torch_zeros((5, nh, hd), cuda), keys, keys, max_seq - 4)
+    out = mlb.attention_rows(torch_zeros((4, nh, hd), cuda), keys, keys, max_seq - 4)
+    assert out.shape == (4, nh, hd)
+
+
+def torch_zeros(shape, device):
+    import torch
+    return torch.zeros(shape, dtype=torch.float32, device=device)
