@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import subprocess
 import math
 import os
 import statistics
@@ -713,6 +714,36 @@ def attention_bench(args):
         torch.cuda.empty_cache()
 
 
+# ---------------------------------------------------------------- prefill
+
+PREFILL_EXE = os.path.join(ROOT, "mini-lla_b200", "host", "_build", "mlb_prefill_bench")
+
+
+def prefill_bench(args):
+    """Whole-model prefill and decode through the C++ layer's
+    ForwardBatchCuda on a random-weight model of Llama-3-8B shape
+    (--prefill-layers layers), beside the reference's per-token GPU driver
+    and its CPU forward pass; one JSON line (the program's)."""
+    if not os.path.exists(PREFILL_EXE):
+        print(json.dumps({"prefill": "unavailable",
+                          "why": "mlb_prefill_bench not built (needs the reference "
+                                 "headers: make -C mini-lla_b200/host)"}))
+        return
+    cmd = [PREFILL_EXE, "--layers", str(args.prefill_layers), "--tokens",
+           str(args.prefill_tokens), "--type", args.prefill_type,
+           "--steps", str(max(1, min(args.steps, 10))), "--warmup", str(max(1, args.warmup)),
+           "--max-rows", str(max(512, args.prefill_tokens))]
+    if args.no_cpu_baseline:
+        cmd += ["--cpu-tokens", "0"]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
+    if res.returncode != 0:
+        raise RuntimeError(f"mlb_prefill_bench failed: {res.stderr[-2000:]}")
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    line.update({"metric": "prefill tokens/s (ForwardBatchCuda, whole layers)",
+                 "data": "synthetic random-weight model", "dtype": "f32 (ggml blocks)"})
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- sweep
 
 SWEEP_OPS = ("rmsnorm", "res_rmsnorm", "swiglu", "emb_q8_0", "emb_q4_0", "emb_q4_1")
@@ -876,6 +907,11 @@ def main():
                     help="decode-path linear layer: one JSON line per shape")
     ap.add_argument("--attention", action="store_true",
                     help="decode attention: one JSON line per case")
+    ap.add_argument("--prefill", action="store_true",
+                    help="whole-model prefill / decode through ForwardBatchCuda")
+    ap.add_argument("--prefill-layers", type=int, default=4)
+    ap.add_argument("--prefill-tokens", type=int, default=512)
+    ap.add_argument("--prefill-type", default="Q8_0")
     ap.add_argument("--linear-qtypes", default="", help="e.g. Q8_0,F32")
     ap.add_argument("--linear-shapes", default="", help="e.g. 14336x4096")
     ap.add_argument("--linear-tokens", default="", help="e.g. 1,4")
@@ -892,6 +928,9 @@ def main():
         return
     if args.attention:
         attention_bench(args)
+        return
+    if args.prefill:
+        prefill_bench(args)
         return
     if args.impl == "reference":
         reference_arm(args, cfg)

@@ -348,6 +348,39 @@ __host__ __device__ constexpr int BlockBytes() {  // bytes per 32 columns
   return QT == MLB_F32 ? 128 : (QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20));
 }
 
+// One group of 4 blocks: lane l takes float4 group l % 8 of block l / 8
+// (blk already points at the lane's block, x at its x float4 of token 0).
+template <int QT, int T>
+__device__ __forceinline__ void BulkGroup(const uint8_t* blk, const float4* x, int k4,
+                                          int lane, uint64_t (&acc)[T]) {
+  if (QT == MLB_F32) {
+    const float4 w = *reinterpret_cast<const float4*>(blk + (lane & 7) * 16);
+    const uint64_t w01 = Pack2(w.x, w.y), w23 = Pack2(w.z, w.w);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const float4 xv = x[t * k4];
+      acc[t] = Fma2(w01, Pack2(xv.x, xv.y), acc[t]);
+      acc[t] = Fma2(w23, Pack2(xv.z, xv.w), acc[t]);
+    }
+  } else {
+    uint64_t q01, q23;
+    QuantPairs<QT>(blk, (lane & 7) * 4, q01, q23);
+    const uint32_t scale =
+        QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(blk) : Smem16(blk);
+    const float d = HalfBits(scale & 0xffffu);
+    const uint64_t d2 = Pack2(d, d);
+    const float m = QT == MLB_Q4_1 ? HalfBits(scale >> 16) : 0.0f;
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const float4 xv = x[t * k4];
+      const uint64_t x01 = Pack2(xv.x, xv.y), x23 = Pack2(xv.z, xv.w);
+      const uint64_t p = Fma2(q23, x23, Mul2(q01, x01));
+      acc[t] = Fma2(d2, p, acc[t]);
+      if (QT == MLB_Q4_1) acc[t] = Fma2(Pack2(m, m), Add2(x01, x23), acc[t]);
+    }
+  }
+}
+
 template <int QT, int T>
 __global__ void __launch_bounds__(kBulkMaxWarps * 32)
     GemvBulkKernel(GemvArgs a, int sb, int slot_bytes) {
@@ -406,9 +439,9 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32)
   };
 
   for (int s = 0; s < kBulkStages - 1 && s < nseg; ++s) issue(s);
-  uint64_t acc[T];
+  uint64_t acc[T], acc2[T];
 #pragma unroll
-  for (int t = 0; t < T; ++t) acc[t] = 0;  // (+0.0f, +0.0f)
+  for (int t = 0; t < T; ++t) acc[t] = acc2[t] = 0;  // (+0.0f, +0.0f)
   int64_t row = w0;
   int kb = 0;  // block index of the current group inside `row`
   for (int s = 0; s < nseg; ++s) {
@@ -426,44 +459,28 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32)
     const int64_t gb = b0 + static_cast<int64_t>(s) * sb;
     const int count = static_cast<int>((gb + sb < b1 ? gb + sb : b1) - gb);
     const uint8_t* slot = ring + (s % kBulkStages) * slot_bytes;
-    for (int b = s == 0 ? static_cast<int>(first - b0) : 0; b < count; b += 4) {
+    int b = s == 0 ? static_cast<int>(first - b0) : 0;
+    while (b < count) {
+      // blocks left in this segment and in the current row (multiples of 4)
+      const int run = count - b < nb - kb ? count - b : nb - kb;
       const uint8_t* blk = slot + (b + (lane >> 3)) * kBB;
-      const int xo = kb * 8 + lane;  // this lane's x float4
-      if (QT == MLB_F32) {
-        const float4 w = *reinterpret_cast<const float4*>(blk + (lane & 7) * 16);
-        const uint64_t w01 = Pack2(w.x, w.y), w23 = Pack2(w.z, w.w);
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 xv = xs[t * k4 + xo];
-          acc[t] = Fma2(w01, Pack2(xv.x, xv.y), acc[t]);
-          acc[t] = Fma2(w23, Pack2(xv.z, xv.w), acc[t]);
-        }
-      } else {
-        uint64_t q01, q23;
-        QuantPairs<QT>(blk, (lane & 7) * 4, q01, q23);
-        const uint32_t scale = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(blk)
-                                              : Smem16(blk);
-        const float d = HalfBits(scale & 0xffffu);
-        const uint64_t d2 = Pack2(d, d);
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 xv = xs[t * k4 + xo];
-          const uint64_t x01 = Pack2(xv.x, xv.y), x23 = Pack2(xv.z, xv.w);
-          const uint64_t p = Fma2(q23, x23, Mul2(q01, x01));
-          acc[t] = Fma2(d2, p, acc[t]);
-          if (QT == MLB_Q4_1) {
-            const float m = HalfBits(scale >> 16);
-            acc[t] = Fma2(Pack2(m, m), Add2(x01, x23), acc[t]);
-          }
-        }
+      const float4* xg = xs + kb * 8 + lane;  // this lane's x float4
+      int i = 0;
+      // two independent groups of 4 blocks per step (ILP across the chains)
+      for (; i + 8 <= run; i += 8) {
+        BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
+        BulkGroup<QT, T>(blk + (i + 4) * kBB, xg + (i + 4) * 8, k4, lane, acc2);
       }
-      kb += 4;
+      if (i < run) BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
+      b += run;
+      kb += run;
       if (kb == nb) {
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-          const float sum = WarpSum(SumPair(acc[t]));
+          const float sum = WarpSum(SumPair(Add2(acc[t], acc2[t])));
           if (lane == t) a.y[static_cast<int64_t>(t) * a.n + row] = sum;
           acc[t] = 0;
+          acc2[t] = 0;
         }
         ++row;
         kb = 0;
