@@ -637,6 +637,10 @@ def gpu_arm(args, cfg):
 LINEAR_SHAPES = ((14336, 4096), (4096, 14336), (4864, 896), (896, 4864))
 
 
+LINEAR_TC_MIN_TOKENS = 48   # mlb_linear_rows_f32 runs on the tensor cores from here
+TF32_DENSE_TFLOPS = 1100.0  # B200 nominal dense TF32 (no measured figure in the pool file)
+
+
 def linear_bench(args):
     """Decode-path linear layer (mlb_linear_f32): one JSON line per
     (format, n, k, tokens) — LLaMA-3-8B FFN gate/up [14336, 4096] and down
@@ -661,18 +665,31 @@ def linear_bench(args):
             for t in tokens:
                 x = torch.randn((t, k), generator=g, device=dev)
                 y = torch.empty((t, n), device=dev)
-                fn = lambda: mlb.linear(w, qt, n, k, x, out=y)  # noqa: E731
+                tc = t >= LINEAR_TC_MIN_TOKENS
+                if tc:  # prompt-sized: the tensor-core entry, scratch preallocated
+                    scratch = torch.empty(mlb.load().mlb_linear_rows_scratch_floats(k, t),
+                                          device=dev)
+                    fn = lambda: mlb.linear_rows(w, qt, n, k, x, out=y,  # noqa: E731
+                                                 scratch=scratch)
+                else:
+                    fn = lambda: mlb.linear(w, qt, n, k, x, out=y)  # noqa: E731
                 nbytes = n * wl.row_bytes(qt, k) + 4 * t * (k + n)
                 ms = time_fn(fn, nbytes, 1)
                 gbs = nbytes / (ms / 1e3) / 1e9
-                print(json.dumps({
+                line = {
                     "linear": wl.QNAME[qt], "n": n, "k": k, "tokens": t,
+                    "path": "tcgen05 tf32x3" if tc else "gemv",
                     "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
                     "frac_of_measured": round(gbs / peak, 4),
                     "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
                     "peak_kind": peak_kind,
-                    "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}),
-                    flush=True)
+                    "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}
+                if tc:  # 3 TF32 products per multiply-add: against the dense TF32 peak
+                    tflops = 3 * 2 * n * k * t / (ms / 1e3) / 1e12
+                    line.update({"tf32_tflops": round(tflops, 1),
+                                 "frac_of_tf32_peak": round(tflops / TF32_DENSE_TFLOPS, 4),
+                                 "fp32_equiv_tflops": round(tflops / 3, 1)})
+                print(json.dumps(line), flush=True)
             del w
             torch.cuda.empty_cache()
 

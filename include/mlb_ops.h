@@ -204,6 +204,26 @@ int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
 int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                    const float* x, int64_t t_rows, float* y, void* stream);
 
+/* Floats of scratch mlb_linear_rows_f32 needs for t_rows tokens of k values
+ * (-1 for bad arguments). */
+int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows);
+
+/*
+ * Linear layer for prompt-sized batches: y[t] = W . x[t] for t < t_rows, the
+ * reference's CudaLinear / Linear (cuda_matmul.cu, quant.cc:171-226) applied
+ * to every token of a prompt at once.  From 48 tokens on (k % 32 == 0,
+ * row_bytes % 16 == 0, 16-byte aligned table and x) it runs on the tensor
+ * cores: tcgen05 TF32 MMAs with W dequantised in shared memory and both
+ * operands split into TF32 head + tail (three products per tile), so the
+ * result stays within 1e-5 * sum|w x| of the reference's fp32 sum; `scratch`
+ * (caller-owned device memory of mlb_linear_rows_scratch_floats(k, t_rows)
+ * floats) holds x's split.  Otherwise it is mlb_linear_f32 (scratch unused).
+ * x [t_rows, k], y [t_rows, n].
+ */
+int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t k,
+                        const float* x, int64_t t_rows, float* y, float* scratch,
+                        int64_t scratch_floats, void* stream);
+
 /*
  * Number of bounded device-side waits (a bulk weight copy that did not land
  * within the kernel's poll limit) that gave up on the current device since

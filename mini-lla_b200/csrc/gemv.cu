@@ -605,11 +605,16 @@ int LaunchVec(const GemvArgs& a, int t_rows, bool bulk_ok, cudaStream_t s) {
 }  // namespace
 }  // namespace mlb
 
+namespace mlb {
+unsigned int TcWaitTimeouts();  // linear_tc.cu
+}  // namespace mlb
+
 extern "C" int mlb_wait_timeouts(unsigned int* count) {
   using namespace mlb;
   if (count == nullptr) return Fail(MLB_ERR_ARG, "mlb_wait_timeouts: null pointer");
   if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
+  *count += TcWaitTimeouts();
   return MLB_OK;
 }
 

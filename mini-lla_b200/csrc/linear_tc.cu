@@ -1,0 +1,513 @@
+// Prompt-sized linear layers on the 5th-generation tensor cores:
+// y[t] = W . x[t] for t < T with W [n, k] in the reference's ggml blocks
+// (Q8_0 / Q4_0 / Q4_1) or F32 and x [T, k] fp32.
+//
+// Reference arithmetic: src/quant.cc:171-226 (LinearWithBlocks) and
+// src/matmul_optimized.cc:95-117 (F32), a sequential fp32 sum of
+// dequant(w_i) * x_i per output; the reference runs it once per token.
+//
+// Accuracy on TF32 tensor cores: every operand is split into a TF32 head and
+// a TF32 tail, w = wh + wl and x = xh + xl, and each tile accumulates
+// wh.xh + wh.xl + wl.xh in fp32 (the dropped wl.xl term and the tail
+// roundings are ~2^-21 of each product).  A dequantised ggml weight d * q
+// has at most 19 significant bits, so wh + wl holds it exactly.  Results
+// match the reference within 1e-5 * sum_i |w_i x_i| (tests).
+//
+// Design (one CTA = 128 weight rows x 128 tokens, k in steps of 32 = one
+// ggml block; 256 threads in warp roles):
+//   - warp 0, one lane: TMA producer.  Per step it loads the raw weight
+//     bytes of the 128 rows (a 2-D uint8 tensor map over [n, row_bytes];
+//     the box starts at the block's byte offset rounded down to 16 and is
+//     64 bytes wide, which covers any 34 / 18 / 20-byte block) and the
+//     128 x 32 tiles of xh and xl (fp32 tensor maps, 128-byte swizzle);
+//   - warps 4-7: dequantisers.  Thread m decodes row m's block, splits it
+//     into TF32 head / tail and writes both into 128 x 32 tiles in the
+//     K-major 128-byte-swizzled layout the MMA reads;
+//   - warp 1, one lane: MMA issuer.  Per step 4 k-slices x 3 products of
+//     tcgen05.mma.cta_group::1.kind::tf32 (M = 128, N = 128, K = 8) into a
+//     128-column fp32 accumulator in tensor memory; tcgen05.commit frees the
+//     stage's buffers;
+//   - warp 2 allocates / frees the tensor memory; warps 4-7 finally read
+//     the accumulator (tcgen05.ld, lane = weight row) and store y[t, row],
+//     32 consecutive rows per warp store.
+// Stages form a ring (3 for the quantised formats, 2 for F32) tracked by
+// mbarriers; every wait is bounded (a wait that gives up is counted in
+// g_tc_wait_timeouts and the CTA writes NaN instead of its tile).
+// x is split into xh / xl by a small kernel first (caller scratch).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace mlb {
+namespace {
+
+constexpr int kTileRows = 128;    // weight rows (MMA M)
+constexpr int kTileTokens = 128;  // tokens (MMA N)
+constexpr int kStepK = 32;        // k per stage: one ggml block
+constexpr int kTcThreads = 256;
+constexpr int kTileBytes = kTileRows * kStepK * 4;  // one 128 x 32 fp32 tile
+constexpr int kTmemColumns = 128;
+
+__host__ __device__ constexpr int TcBlockBytes(int qt) {
+  return qt == MLB_F32 ? 128 : (qt == MLB_Q8_0 ? 34 : (qt == MLB_Q4_0 ? 18 : 20));
+}
+__host__ __device__ constexpr int TcRawBytes(int qt) { return qt == MLB_F32 ? 128 : 64; }
+__host__ __device__ constexpr int TcStages(int qt) { return qt == MLB_F32 ? 2 : 3; }
+
+// Shared-memory layout from a 1024-byte aligned base: per stage four tiles
+// (A head, A tail, B head, B tail), then the raw weight tiles, then the
+// mbarriers (full, dequantised, empty per stage; accumulator ready) and the
+// tensor-memory address.
+__host__ __device__ constexpr int TcRawOffset(int qt) { return TcStages(qt) * 4 * kTileBytes; }
+__host__ __device__ constexpr int TcBarOffset(int qt) {
+  return TcRawOffset(qt) + TcStages(qt) * kTileRows * TcRawBytes(qt);
+}
+__host__ __device__ constexpr int TcSmemBytes(int qt) {
+  return TcBarOffset(qt) + 8 * (3 * TcStages(qt) + 1) + 16 + 1024;  // + alignment slack
+}
+
+__device__ __forceinline__ uint32_t SmemU32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void MbarInit(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void MbarExpectTx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void MbarArrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool MbarTryWait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(1000)
+      : "memory");
+  return ok != 0;
+}
+// ~2 s at most (each poll suspends for at most ~1 us)
+__device__ __forceinline__ bool MbarWait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 21); ++i)
+    if (MbarTryWait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void TmaLoad2D(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
+// 8-row atoms of 128-byte rows 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t SmemDesc(uint32_t addr) {
+  uint64_t d = static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;            // LBO (unused when swizzled)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;    // SBO
+  d |= static_cast<uint64_t>(1) << 46;            // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D fp32, A and B TF32, both K-major, N = 128, M = 128.
+constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) |
+                                (static_cast<uint32_t>(kTileTokens >> 3) << 17) |
+                                (static_cast<uint32_t>(kTileRows >> 4) << 24);
+
+__device__ __forceinline__ void MmaTf32(uint32_t tmem, uint64_t a, uint64_t b,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kInstrDesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void MmaCommit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ float Tf32(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// Row m's 32 weights of the current block (the reference's dequantised
+// values: d * q, d * (n - 8), d * n + m, or the F32 value).
+template <int QT>
+__device__ __forceinline__ void DequantRow(const uint8_t* p, float (&w)[32]) {
+  if (QT == MLB_F32) {
+    const float4* f = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 v = f[c];
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    return;
+  }
+  const float d = Fp16BitsToF32(*reinterpret_cast<const uint16_t*>(p));
+  if (QT == MLB_Q8_0) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t two = *reinterpret_cast<const uint16_t*>(p + 2 + 2 * i);
+      w[2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(two & 0xFF)));
+      w[2 * i + 1] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(two >> 8)));
+    }
+  } else if (QT == MLB_Q4_0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t two = *reinterpret_cast<const uint16_t*>(p + 2 + 2 * i);
+      w[2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>(two & 15) - 8));
+      w[2 * i + 1] = __fmul_rn(d, static_cast<float>(static_cast<int>((two >> 8) & 15) - 8));
+      w[16 + 2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>((two >> 4) & 15) - 8));
+      w[17 + 2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>(two >> 12) - 8));
+    }
+  } else {
+    const float mn = Fp16BitsToF32(*reinterpret_cast<const uint16_t*>(p + 2));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t four = *reinterpret_cast<const uint32_t*>(p + 4 + 4 * i);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t byte = (four >> (8 * b)) & 0xFF;
+        w[4 * i + b] = __fadd_rn(__fmul_rn(d, static_cast<float>(byte & 15)), mn);
+        w[16 + 4 * i + b] = __fadd_rn(__fmul_rn(d, static_cast<float>(byte >> 4)), mn);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+// Bounded waits of the tensor-core linear kernel that gave up.
+__device__ unsigned int g_tc_wait_timeouts;
+
+namespace {
+
+template <int QT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    LinearTcKernel(const __grid_constant__ CUtensorMap wmap,
+                   const __grid_constant__ CUtensorMap xhmap,
+                   const __grid_constant__ CUtensorMap xlmap, float* __restrict__ y, int n,
+                   int t_rows, int k) {
+  constexpr int S = TcStages(QT);
+  constexpr int kRaw = TcRawBytes(QT);
+  constexpr int kBB = TcBlockBytes(QT);
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // 1024-byte aligned base (the swizzled tiles need it)
+  const uint32_t raw_addr = SmemU32(smem_raw);
+  uint8_t* base = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = SmemU32(base);
+  auto a_hi = [&](int s) { return sbase + s * 4 * kTileBytes; };
+  auto a_lo = [&](int s) { return sbase + s * 4 * kTileBytes + kTileBytes; };
+  auto b_hi = [&](int s) { return sbase + s * 4 * kTileBytes + 2 * kTileBytes; };
+  auto b_lo = [&](int s) { return sbase + s * 4 * kTileBytes + 3 * kTileBytes; };
+  uint8_t* raw = base + TcRawOffset(QT);
+  const uint32_t bars = sbase + TcBarOffset(QT);
+  auto full = [&](int s) { return bars + 8 * s; };
+  auto dequantised = [&](int s) { return bars + 8 * (S + s); };
+  auto empty = [&](int s) { return bars + 8 * (2 * S + s); };
+  const uint32_t acc_ready = bars + 8 * (3 * S);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + TcBarOffset(QT) + 8 * (3 * S + 1));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTileRows;
+  const int t0 = blockIdx.y * kTileTokens;
+  const int steps = k / kStepK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      MbarInit(full(s), 1);
+      MbarInit(dequantised(s), kTileRows);
+      MbarInit(empty(s), 1);
+    }
+    MbarInit(acc_ready, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     SmemU32(tmem_slot)),
+                 "r"(kTmemColumns)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  int issued = 0;  // producer: stages whose loads were issued
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < steps; ++s) {
+        const int slot = s % S;
+        if (!MbarWait(empty(slot), ((s / S) & 1) ^ 1) || *abort_flag) {
+          atomicAdd(&g_tc_wait_timeouts, 1u);
+          *abort_flag = 1;
+          break;
+        }
+        MbarExpectTx(full(slot), kTileRows * kRaw + 2 * kTileBytes);
+        const int xw = (s * kBB) & ~15;  // byte column of the block, rounded down
+        TmaLoad2D(SmemU32(raw + slot * kTileRows * kRaw), &wmap, xw, n0, full(slot));
+        TmaLoad2D(b_hi(slot), &xhmap, s * kStepK, t0, full(slot));
+        TmaLoad2D(b_lo(slot), &xlmap, s * kStepK, t0, full(slot));
+        issued = s + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int s = 0; s < steps; ++s) {
+        const int slot = s % S;
+        if (!MbarWait(dequantised(slot), (s / S) & 1) || *abort_flag) {
+          atomicAdd(&g_tc_wait_timeouts, 1u);
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < kStepK / 8; ++j) {  // K = 8 TF32 = 32 bytes per MMA
+          const uint64_t ah = SmemDesc(a_hi(slot) + 32 * j);
+          const uint64_t al = SmemDesc(a_lo(slot) + 32 * j);
+          const uint64_t bh = SmemDesc(b_hi(slot) + 32 * j);
+          const uint64_t bl = SmemDesc(b_lo(slot) + 32 * j);
+          MmaTf32(tmem, ah, bh, (s | j) != 0 ? 1u : 0u);
+          MmaTf32(tmem, ah, bl, 1u);
+          MmaTf32(tmem, al, bh, 1u);
+        }
+        MmaCommit(empty(slot));  // the stage's buffers are free once these finish
+      }
+      MmaCommit(acc_ready);  // every MMA issued so far has finished
+    }
+  } else if (warp >= 4) {
+    const int m = threadIdx.x - 128;  // weight row within the tile
+    for (int s = 0; s < steps; ++s) {
+      const int slot = s % S;
+      if (!MbarWait(full(slot), (s / S) & 1) || *abort_flag) {
+        atomicAdd(&g_tc_wait_timeouts, 1u);
+        *abort_flag = 1;
+        break;
+      }
+      float w[32];
+      DequantRow<QT>(raw + slot * kTileRows * kRaw + m * kRaw + ((s * kBB) & 15), w);
+      uint8_t* hi = base + (a_hi(slot) - sbase) + m * 128;
+      uint8_t* lo = base + (a_lo(slot) - sbase) + m * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float4 h, l;
+        h.x = Tf32(w[4 * c]);
+        h.y = Tf32(w[4 * c + 1]);
+        h.z = Tf32(w[4 * c + 2]);
+        h.w = Tf32(w[4 * c + 3]);
+        l.x = Tf32(w[4 * c] - h.x);
+        l.y = Tf32(w[4 * c + 1] - h.y);
+        l.z = Tf32(w[4 * c + 2] - h.z);
+        l.w = Tf32(w[4 * c + 3] - h.w);
+        const int chunk = (c ^ (m & 7)) << 4;  // 128-byte swizzle
+        *reinterpret_cast<float4*>(hi + chunk) = h;
+        *reinterpret_cast<float4*>(lo + chunk) = l;
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      MbarArrive(dequantised(slot));
+    }
+    // epilogue: lane = weight row, column = token
+    const bool ok = MbarWait(acc_ready, 0) && !*abort_flag;
+    if (!ok && lane == 0) atomicAdd(&g_tc_wait_timeouts, 1u);
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const int row = n0 + m;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < kTileTokens; c += 16) {
+      uint32_t v[16];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+          " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+            "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+            "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          : "r"(taddr + c));
+      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+      if (row < n) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + c + j;
+          if (t < t_rows)
+            y[static_cast<int64_t>(t) * n + row] = ok ? __uint_as_float(v[j]) : __int_as_float(0x7fc00000);
+        }
+      }
+    }
+  }
+  // let any load still in flight land before the CTA leaves (only after a
+  // timeout can a consumer have stopped early)
+  __syncthreads();
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    for (int s = issued - S > 0 ? issued - S : 0; s < issued; ++s)
+      MbarWait(full(s % S), (s / S) & 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  if (warp == 2) {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                 "r"(kTmemColumns)
+                 : "memory");
+  }
+}
+
+// x -> TF32 head and tail, one float4 per thread.
+__global__ void __launch_bounds__(256)
+    SplitTf32Kernel(const float4* __restrict__ x, float4* __restrict__ xh,
+                    float4* __restrict__ xl, int64_t count4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= count4) return;
+  const float4 v = x[i];
+  float4 h, l;
+  h.x = Tf32(v.x);
+  h.y = Tf32(v.y);
+  h.z = Tf32(v.z);
+  h.w = Tf32(v.w);
+  l.x = Tf32(v.x - h.x);
+  l.y = Tf32(v.y - h.y);
+  l.z = Tf32(v.z - h.z);
+  l.w = Tf32(v.w - h.w);
+  xh[i] = h;
+  xl[i] = l;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+bool Map2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner,
+           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+           CUtensorMapSwizzle swizzle) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = EncodeFn();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, type, 2, const_cast<void*>(base), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int QT>
+int LaunchTc(const void* w, int64_t n, int64_t k, int64_t row_bytes, const float* xh,
+             const float* xl, int64_t t_rows, float* y, cudaStream_t s) {
+  CUtensorMap wmap, xhmap, xlmap;
+  if (!Map2D(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(row_bytes),
+             static_cast<uint64_t>(n), static_cast<uint64_t>(row_bytes), TcRawBytes(QT),
+             kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !Map2D(&xhmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xh, static_cast<uint64_t>(k),
+             static_cast<uint64_t>(t_rows), static_cast<uint64_t>(k) * 4, kStepK, kTileTokens,
+             CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !Map2D(&xlmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xl, static_cast<uint64_t>(k),
+             static_cast<uint64_t>(t_rows), static_cast<uint64_t>(k) * 4, kStepK, kTileTokens,
+             CU_TENSOR_MAP_SWIZZLE_128B))
+    return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: tensor map encoding failed");
+  auto kernel = LinearTcKernel<QT>;
+  constexpr int shm = TcSmemBytes(QT);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shm) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: shared memory opt-in");
+  }
+  const dim3 grid(static_cast<unsigned>((n + kTileRows - 1) / kTileRows),
+                  static_cast<unsigned>((t_rows + kTileTokens - 1) / kTileTokens));
+  kernel<<<grid, kTcThreads, shm, s>>>(wmap, xhmap, xlmap, y, static_cast<int>(n),
+                                       static_cast<int>(t_rows), static_cast<int>(k));
+  return CheckLaunch("mlb_linear_rows_f32");
+}
+
+}  // namespace
+
+// Host side of mlb_wait_timeouts for this file's kernels.
+unsigned int TcWaitTimeouts() {
+  unsigned int count = 0;
+  if (cudaMemcpyFromSymbol(&count, g_tc_wait_timeouts, sizeof(count)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return count;
+}
+
+}  // namespace mlb
+
+// Token counts from which the tensor-core form is used (below it the GEMV
+// form of mlb_linear_f32 reads every weight once per 8 tokens and wins).
+static constexpr int64_t kTcMinTokens = 48;
+
+extern "C" int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows) {
+  if (k <= 0 || t_rows < 0) return -1;
+  return 2 * k * t_rows + 8;  // xh, xl (+ room to align each to 16 bytes)
+}
+
+extern "C" int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t k,
+                                   const float* x, int64_t t_rows, float* y, float* scratch,
+                                   int64_t scratch_floats, void* stream) {
+  using namespace mlb;
+  if (qtype < MLB_F32 || qtype > MLB_Q4_1)
+    return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: unknown qtype");
+  if (n < 0 || k <= 0 || k > INT_MAX || t_rows < 0 || n > INT_MAX || t_rows > INT_MAX)
+    return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: bad shape");
+  if (n == 0 || t_rows == 0) return MLB_OK;
+  const int64_t row_bytes = mlb_row_bytes(qtype, k);
+  const uintptr_t wp = reinterpret_cast<uintptr_t>(w);
+  const bool tc = t_rows >= kTcMinTokens && (k % kStepK) == 0 && (row_bytes % 16) == 0 &&
+                  (wp & 15u) == 0 && w != nullptr && x != nullptr && Aligned16(x);
+  if (!tc) return mlb_linear_f32(w, qtype, n, k, x, t_rows, y, stream);
+  if (y == nullptr) return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: null pointer");
+  if (scratch == nullptr || scratch_floats < mlb_linear_rows_scratch_floats(k, t_rows))
+    return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: scratch too small");
+  float* xh = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t{15});
+  float* xl = xh + k * t_rows;  // k % 32 == 0: still 16-byte aligned
+  cudaStream_t s = AsStream(stream);
+  const int64_t count4 = k * t_rows / 4;
+  SplitTf32Kernel<<<static_cast<unsigned>((count4 + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(xh),
+      reinterpret_cast<float4*>(xl), count4);
+  int rc = CheckLaunch("mlb_linear_rows_f32");
+  if (rc != MLB_OK) return rc;
+  switch (qtype) {
+    case MLB_F32: return LaunchTc<MLB_F32>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
+    case MLB_Q8_0: return LaunchTc<MLB_Q8_0>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
+    case MLB_Q4_0: return LaunchTc<MLB_Q4_0>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
+    case MLB_Q4_1: return LaunchTc<MLB_Q4_1>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
+  }
+  return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: unknown qtype");
+}

@@ -1,9 +1,10 @@
 // mini-lla's device linear layer (the reference's
-// include/mini_llama/cuda_matmul.h) over libmlb.so's mlb_linear_f32.  This
-// file takes the place of the reference's src/cuda_matmul.cu: the F32 path no
-// longer needs cuBLAS, and the Q8_0 / Q4_0 / Q4_1 paths stage each weight
-// row with 16-byte loads and reduce it across a warp instead of running one
-// thread per output row.
+// include/mini_llama/cuda_matmul.h) over libmlb.so's mlb_linear_f32, and its
+// row-batched form CudaLinearRows over mlb_linear_rows_f32.  This file takes
+// the place of the reference's src/cuda_matmul.cu: the F32 path no longer
+// needs cuBLAS, the Q8_0 / Q4_0 / Q4_1 decode paths stream each weight row
+// through shared memory and reduce it across a warp instead of running one
+// thread per output row, and prompt-sized batches run on the tensor cores.
 #include "mini_llama/cuda_matmul.h"
 
 #include <cstdint>
@@ -55,7 +56,21 @@ CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight) {
   }
   const int rows = static_cast<int>(x.Size() / static_cast<size_t>(weight.cols));
   CudaTensor output({rows, weight.rows});
-  if (rows > 0) Linear(x, weight, rows, &output, "CudaLinearRows");
+  if (rows == 0) return output;
+  // prompt-sized batches run on the tensor cores; their scratch (x split
+  // into TF32 head and tail) comes from the pool, ordered on the default
+  // stream like every other operator's buffers
+  const int64_t need = mlb_linear_rows_scratch_floats(weight.cols, rows);
+  DeviceBuffer scratch;
+  scratch.Reset(static_cast<size_t>(need) * sizeof(float));
+  const int rc = mlb_linear_rows_f32(weight.buffer.data(), QType(weight.type), weight.rows,
+                                     weight.cols, x.data(), rows, output.data(),
+                                     static_cast<float*>(scratch.data()), need, nullptr);
+  if (rc != MLB_OK) {
+    const std::string message = std::string("CudaLinearRows: ") + mlb_last_error();
+    if (rc == MLB_ERR_ARG) throw std::invalid_argument(message);
+    throw std::runtime_error(message);
+  }
   return output;
 }
 

@@ -149,7 +149,8 @@ void TestModel(const ModelSpec& spec, std::mt19937& rng) {
              3u - (spec.tied ? 1u : 0u) + spec.layers * (spec.biases ? 12u : 9u),
          tag + "weight count");
 
-  const int prompt = std::min(37, spec.max_seq - 8);
+  // long enough for the tensor-core linears (48 tokens and more)
+  const int prompt = std::min(100, spec.max_seq - 8);
   const std::vector<int> tokens = Tokens(prompt, spec.vocab, rng);
   Context c_cpu(cpu.config), c_gpu(gpu.config), c_step(gpu.config);
 
@@ -305,15 +306,18 @@ int main() {
   try {
     const ModelSpec specs[] = {
         // bulk-copy GEMV path (k % 128 == 0), GQA 4, untied, normal RoPE
-        {"q8_0 gqa", 300, 256, 512, 2, 8, 2, 64, QuantType::kQ8_0, RopeType::kNormal,
+        {"q8_0 gqa", 300, 256, 512, 2, 8, 2, 128, QuantType::kQ8_0, RopeType::kNormal,
          false, false},
         // biases, NeoX, tied output, MHA
-        {"q4_1 neox bias tied", 200, 128, 384, 2, 4, 4, 64, QuantType::kQ4_1,
+        {"q4_1 neox bias tied", 200, 128, 384, 2, 4, 4, 128, QuantType::kQ4_1,
          RopeType::kNeoX, true, true},
         // k % 128 != 0: the chunked GEMV form; group of 5
-        {"q4_0 group5", 150, 160, 224, 2, 5, 1, 64, QuantType::kQ4_0, RopeType::kNormal,
+        {"q4_0 group5", 150, 160, 224, 2, 5, 1, 128, QuantType::kQ4_0, RopeType::kNormal,
          true, false},
-        {"f32", 120, 128, 256, 1, 4, 2, 64, QuantType::kF32, RopeType::kNormal, false, false},
+        {"f32", 120, 128, 256, 1, 4, 2, 128, QuantType::kF32, RopeType::kNormal, false, false},
+        // a short prompt (the GEMV linears) on a small context
+        {"q8_0 short", 100, 128, 256, 1, 4, 1, 40, QuantType::kQ8_0, RopeType::kNeoX, true,
+         true},
     };
     for (const ModelSpec& spec : specs) TestModel(spec, rng);
     TestValidation(rng);

@@ -51,6 +51,9 @@ SIGNATURES = {
                                      c_void_p]),
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
     "mlb_wait_timeouts": (c_int, [c_void_p]),
+    "mlb_linear_rows_scratch_floats": (c_int64, [c_int64, c_int64]),
+    "mlb_linear_rows_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
+                                    c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
     "mlb_attention_rows_scratch_floats": (c_int64, [c_int, c_int, c_int, c_int64,
                                                     c_int64]),
     "mlb_attention_rows_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
@@ -398,6 +401,30 @@ def attention_rows(q, keys, values, position: int, out=None, scratch=None,
     _check(load().mlb_attention_rows_f32(
         _ptr(q), _ptr(keys), _ptr(values), _ptr(out), int(position), rows, max_seq,
         nh, kvh, hd, _ptr(scratch), scratch.numel(), _stream(stream)), op)
+    return out
+
+
+def linear_rows(weight, qtype: int, n: int, k: int, x, out=None, scratch=None,
+                stream=None):
+    """y = x . dequant(W)^T for x [T, k] -> [T, n]; tensor cores from 48
+    tokens on (mlb_linear_rows_f32)."""
+    import torch
+    op = "linear_rows"
+    _require(weight.is_cuda and weight.is_contiguous(), op,
+             "weight must be a contiguous CUDA tensor")
+    _require(weight.numel() * weight.element_size() >= n * row_bytes(qtype, k), op,
+             "weight smaller than n rows")
+    _f32_cuda(x, op, "x")
+    _require(x.shape[-1] == k, op, "input size mismatch")
+    t_rows = x.numel() // k
+    if out is None:
+        out = torch.empty((t_rows, n), dtype=torch.float32, device=x.device)
+    need = load().mlb_linear_rows_scratch_floats(k, t_rows)
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.float32, device=x.device)
+    _check(load().mlb_linear_rows_f32(_ptr(weight), qtype, n, k, _ptr(x), t_rows,
+                                      _ptr(out), _ptr(scratch), scratch.numel(),
+                                      _stream(stream)), op)
     return out
 
 

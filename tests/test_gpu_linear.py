@@ -85,3 +85,38 @@ def test_linear_rejects_bad_input(cuda):
         mlb.linear(w, wl.Q8_0, 3, 1024, torch.zeros(1024, device=cuda))
     with pytest.raises(ValueError):
         mlb.linear(w, wl.Q8_0, 1, 64, torch.zeros(63, device=cuda))
+
+
+@pytest.mark.parametrize("qtype", [wl.F32, wl.Q8_0, wl.Q4_0, wl.Q4_1])
+@pytest.mark.parametrize("n,k,t", [(128, 256, 48), (300, 4096, 49), (64, 1024, 128),
+                                   (200, 512, 200), (129, 3584, 64), (1000, 4096, 257)])
+def test_linear_rows_tensor_cores_vs_oracle(cuda, oracle, qtype, n, k, t):
+    """Prompt-sized batches (>= 48 tokens) run on the tcgen05 TF32 path with
+    head + tail splits; same 1e-5 * sum|w x| bar as the GEMV, every output
+    (ragged tiles in both n and t included)."""
+    import torch
+    rng = np.random.default_rng(n + 3 * k + 7 * t)
+    table = wl.numpy_quant_table(qtype, n, k, seed=n + k + t)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear_rows(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"rows {wl.QNAME[qtype]} n={n} k={k} t={t}")
+
+
+def test_linear_rows_large_values_and_small_batches(cuda, oracle):
+    """x spanning many binades (the tail split matters) and batches below the
+    tensor-core threshold (the GEMV path) through the same entry."""
+    import torch
+    rng = np.random.default_rng(9)
+    n, k = 256, 1024
+    table = wl.numpy_quant_table(wl.Q8_0, n, k, seed=5)
+    wdeq, _ = oracle.embedding(table, wl.Q8_0, n, k, np.arange(n, dtype=np.int32))
+    for t in (1, 47, 48, 96):
+        x = (rng.standard_normal((t, k)) * np.exp(rng.uniform(-8, 8, (t, k)))).astype(np.float32)
+        want = oracle.linear(table, wl.Q8_0, n, k, x)
+        got = mlb.linear_rows(dev(table, cuda), wl.Q8_0, n, k, dev(x, cuda))
+        torch.cuda.synchronize()
+        _check(got.cpu().numpy(), want, wdeq, x, f"rows wide-range t={t}")
