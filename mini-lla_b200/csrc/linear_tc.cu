@@ -6,36 +6,42 @@
 // src/matmul_optimized.cc:95-117 (F32), a sequential fp32 sum of
 // dequant(w_i) * x_i per output; the reference runs it once per token.
 //
-// Accuracy on TF32 tensor cores: every operand is split into a TF32 head and
-// a TF32 tail, w = wh + wl and x = xh + xl, and each tile accumulates
-// wh.xh + wh.xl + wl.xh in fp32 (the dropped wl.xl term and the tail
-// roundings are ~2^-21 of each product).  A dequantised ggml weight d * q
-// has at most 19 significant bits, so wh + wl holds it exactly.  Results
+// Accuracy on TF32 tensor cores: every operand is split into a TF32 head
+// (its top 19 bits) and the exact remainder, w = wh + wl and x = xh + xl,
+// and each tile accumulates wh.xh + wh.xl + wl.xh in fp32 (the dropped
+// wl.xl term and the TF32 reading of the tails are ~2^-21 of each product).
+// A dequantised ggml weight d * q has at most 19 significant bits, so its
+// tail is exact in TF32 too.  Results
 // match the reference within 1e-5 * sum_i |w_i x_i| (tests).
 //
 // Design (one CTA = 128 weight rows x 128 tokens, k in steps of 32 = one
-// ggml block; 256 threads in warp roles):
-//   - warp 0, one lane: TMA producer.  Per step it loads the raw weight
+// ggml block; 352 threads in warp roles):
+//   - warp 8, one lane: TMA producer.  Per step it loads the raw weight
 //     bytes of the 128 rows (a 2-D uint8 tensor map over [n, row_bytes];
 //     the box starts at the block's byte offset rounded down to 16 and is
 //     64 bytes wide, which covers any 34 / 18 / 20-byte block) and the
 //     128 x 32 tiles of xh and xl (fp32 tensor maps, 128-byte swizzle);
-//   - warps 4-7: dequantisers.  Thread m decodes row m's block, splits it
-//     into TF32 head / tail and writes both into 128 x 32 tiles in the
-//     K-major 128-byte-swizzled layout the MMA reads;
-//   - warp 1, one lane: MMA issuer.  Per step 4 k-slices x 3 products of
+//   - warps 0-7: dequantisers, two threads per weight row (16 values each).
+//     A thread decodes its half of row m's block (byte permutes into the
+//     mantissa of 2^23 instead of int->float conversions, packed f32x2
+//     arithmetic), splits each value into its TF32 head (the top 19 bits,
+//     a mask) and the exact remainder, and writes both into 128 x 32 tiles
+//     in the K-major 128-byte-swizzled layout the MMA reads;
+//   - warp 9, one lane: MMA issuer.  Per step 4 k-slices x 3 products of
 //     tcgen05.mma.cta_group::1.kind::tf32 (M = 128, N = 128, K = 8) into a
 //     128-column fp32 accumulator in tensor memory; tcgen05.commit frees the
 //     stage's buffers;
-//   - warp 2 allocates / frees the tensor memory; warps 4-7 finally read
-//     the accumulator (tcgen05.ld, lane = weight row) and store y[t, row],
-//     32 consecutive rows per warp store.
+//   - warp 10 allocates / frees the tensor memory; warps 0-7 finally read
+//     the accumulator (tcgen05.ld, lane = weight row; warps w and w + 4
+//     share TMEM lanes 32w.. and take one half of the tokens each) and store
+//     y[t, row], 32 consecutive rows per warp store.
 // Stages form a ring (3 for the quantised formats, 2 for F32) tracked by
 // mbarriers; every wait is bounded (a wait that gives up is counted in
 // g_tc_wait_timeouts and the CTA writes NaN instead of its tile).
 // x is split into xh / xl by a small kernel first (caller scratch).
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 
 #include <climits>
 #include <cstdint>
@@ -50,7 +56,8 @@ namespace {
 constexpr int kTileRows = 128;    // weight rows (MMA M)
 constexpr int kTileTokens = 128;  // tokens (MMA N)
 constexpr int kStepK = 32;        // k per stage: one ggml block
-constexpr int kTcThreads = 256;
+constexpr int kTcThreads = 352;       // 8 dequant/epilogue warps + producer, MMA, TMEM
+constexpr int kDequantThreads = 256;  // two per weight row
 constexpr int kTileBytes = kTileRows * kStepK * 4;  // one 128 x 32 fp32 tile
 constexpr int kTmemColumns = 128;
 
@@ -144,20 +151,56 @@ __device__ __forceinline__ void MmaCommit(uint32_t bar) {
       : "memory");
 }
 
-__device__ __forceinline__ float Tf32(float v) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return __uint_as_float(r);
+// TF32 head of an fp32 value: sign, exponent and the top 10 mantissa bits
+// (truncation).  The tail v - head is exact and has at most 13 significant
+// bits; the tensor core reads it as TF32 (dropping at most 2^-11 of it).
+__device__ __forceinline__ uint32_t Tf32Head(uint32_t bits) { return bits & 0xFFFFE000u; }
+
+__device__ __forceinline__ uint64_t Pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 Unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t Add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t Mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
-// Row m's 32 weights of the current block (the reference's dequantised
-// values: d * q, d * (n - 8), d * n + m, or the F32 value).
+// Four bytes -> four exact floats (byte permuted into the low mantissa of
+// 2^23, then `bias` = 2^23 + offset subtracted, two lanes at a time).
+__device__ __forceinline__ void BytesToFloats(uint32_t u, float bias, uint64_t& p01,
+                                              uint64_t& p23) {
+  const uint64_t nb = Pack2(-bias, -bias);
+  p01 = Add2(Pack2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                   __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), nb);
+  p23 = Add2(Pack2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                   __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), nb);
+}
+
+__device__ __forceinline__ uint32_t Lds16(const uint8_t* p) {
+  return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// Half `half` (values 16 * half .. 16 * half + 15) of the block at p, as the
+// reference dequantises them (d * q, d * (n - 8), d * n + m, or the F32
+// value), four values per word of w.
 template <int QT>
-__device__ __forceinline__ void DequantRow(const uint8_t* p, float (&w)[32]) {
+__device__ __forceinline__ void DequantHalf(const uint8_t* p, int half, float (&w)[16]) {
   if (QT == MLB_F32) {
-    const float4* f = reinterpret_cast<const float4*>(p);
+    const float4* f = reinterpret_cast<const float4*>(p + 64 * half);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       const float4 v = f[c];
       w[4 * c] = v.x;
       w[4 * c + 1] = v.y;
@@ -166,35 +209,43 @@ __device__ __forceinline__ void DequantRow(const uint8_t* p, float (&w)[32]) {
     }
     return;
   }
-  const float d = Fp16BitsToF32(*reinterpret_cast<const uint16_t*>(p));
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(Lds16(p))));
+  const uint64_t d2 = Pack2(d, d);
+  uint32_t words[4];
   if (QT == MLB_Q8_0) {
+    const uint8_t* q = p + 2 + 16 * half;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t two = *reinterpret_cast<const uint16_t*>(p + 2 + 2 * i);
-      w[2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(two & 0xFF)));
-      w[2 * i + 1] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(two >> 8)));
-    }
-  } else if (QT == MLB_Q4_0) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t two = *reinterpret_cast<const uint16_t*>(p + 2 + 2 * i);
-      w[2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>(two & 15) - 8));
-      w[2 * i + 1] = __fmul_rn(d, static_cast<float>(static_cast<int>((two >> 8) & 15) - 8));
-      w[16 + 2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>((two >> 4) & 15) - 8));
-      w[17 + 2 * i] = __fmul_rn(d, static_cast<float>(static_cast<int>(two >> 12) - 8));
-    }
+    for (int i = 0; i < 4; ++i)
+      words[i] = (Lds16(q + 4 * i) | (Lds16(q + 4 * i + 2) << 16)) ^ 0x80808080u;
   } else {
-    const float mn = Fp16BitsToF32(*reinterpret_cast<const uint16_t*>(p + 2));
+    const uint8_t* q = p + (QT == MLB_Q4_0 ? 2 : 4);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t four = *reinterpret_cast<const uint32_t*>(p + 4 + 4 * i);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (four >> (8 * b)) & 0xFF;
-        w[4 * i + b] = __fadd_rn(__fmul_rn(d, static_cast<float>(byte & 15)), mn);
-        w[16 + 4 * i + b] = __fadd_rn(__fmul_rn(d, static_cast<float>(byte >> 4)), mn);
-      }
+      const uint32_t u = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(q + 4 * i)
+                                        : (Lds16(q + 4 * i) | (Lds16(q + 4 * i + 2) << 16));
+      words[i] = (half ? u >> 4 : u) & 0x0F0F0F0Fu;
     }
+  }
+  const float bias = QT == MLB_Q8_0 ? 8388736.0f : (QT == MLB_Q4_0 ? 8388616.0f : 8388608.0f);
+  const float mn = QT == MLB_Q4_1
+                       ? __half2float(__ushort_as_half(static_cast<unsigned short>(Lds16(p + 2))))
+                       : 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t a, b;
+    BytesToFloats(words[i], bias, a, b);
+    a = Mul2(a, d2);  // exact: 11-bit scale times a code of at most 8 bits
+    b = Mul2(b, d2);
+    if (QT == MLB_Q4_1) {  // d * n + m, rounded like the reference's sum
+      const uint64_t m2 = Pack2(mn, mn);
+      a = Add2(a, m2);
+      b = Add2(b, m2);
+    }
+    const float2 fa = Unpack2(a), fb = Unpack2(b);
+    w[4 * i] = fa.x;
+    w[4 * i + 1] = fa.y;
+    w[4 * i + 2] = fb.x;
+    w[4 * i + 3] = fb.y;
   }
 }
 
@@ -241,14 +292,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       MbarInit(full(s), 1);
-      MbarInit(dequantised(s), kTileRows);
+      MbarInit(dequantised(s), kDequantThreads);
       MbarInit(empty(s), 1);
     }
     MbarInit(acc_ready, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 2) {
+  if (warp == 10) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      SmemU32(tmem_slot)),
                  "r"(kTmemColumns)
@@ -261,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   int issued = 0;  // producer: stages whose loads were issued
-  if (warp == 0) {
+  if (warp == 8) {
     if (lane == 0) {
       for (int s = 0; s < steps; ++s) {
         const int slot = s % S;
@@ -278,7 +329,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         issued = s + 1;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     if (lane == 0) {
       for (int s = 0; s < steps; ++s) {
         const int slot = s % S;
@@ -302,8 +353,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       MmaCommit(acc_ready);  // every MMA issued so far has finished
     }
-  } else if (warp >= 4) {
-    const int m = threadIdx.x - 128;  // weight row within the tile
+  } else if (warp < 8) {
+    const int m = threadIdx.x & (kTileRows - 1);  // weight row within the tile
+    const int half = threadIdx.x >> 7;             // which 16 values of the block
     for (int s = 0; s < steps; ++s) {
       const int slot = s % S;
       if (!MbarWait(full(slot), (s / S) & 1) || *abort_flag) {
@@ -311,36 +363,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         *abort_flag = 1;
         break;
       }
-      float w[32];
-      DequantRow<QT>(raw + slot * kTileRows * kRaw + m * kRaw + ((s * kBB) & 15), w);
+      float w[16];
+      DequantHalf<QT>(raw + slot * kTileRows * kRaw + m * kRaw + ((s * kBB) & 15), half, w);
       uint8_t* hi = base + (a_hi(slot) - sbase) + m * 128;
       uint8_t* lo = base + (a_lo(slot) - sbase) + m * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float4 h, l;
-        h.x = Tf32(w[4 * c]);
-        h.y = Tf32(w[4 * c + 1]);
-        h.z = Tf32(w[4 * c + 2]);
-        h.w = Tf32(w[4 * c + 3]);
-        l.x = Tf32(w[4 * c] - h.x);
-        l.y = Tf32(w[4 * c + 1] - h.y);
-        l.z = Tf32(w[4 * c + 2] - h.z);
-        l.w = Tf32(w[4 * c + 3] - h.w);
-        const int chunk = (c ^ (m & 7)) << 4;  // 128-byte swizzle
-        *reinterpret_cast<float4*>(hi + chunk) = h;
-        *reinterpret_cast<float4*>(lo + chunk) = l;
+      for (int j = 0; j < 4; ++j) {
+        uint4 h, l;
+        h.x = Tf32Head(__float_as_uint(w[4 * j]));
+        h.y = Tf32Head(__float_as_uint(w[4 * j + 1]));
+        h.z = Tf32Head(__float_as_uint(w[4 * j + 2]));
+        h.w = Tf32Head(__float_as_uint(w[4 * j + 3]));
+        l.x = __float_as_uint(w[4 * j] - __uint_as_float(h.x));
+        l.y = __float_as_uint(w[4 * j + 1] - __uint_as_float(h.y));
+        l.z = __float_as_uint(w[4 * j + 2] - __uint_as_float(h.z));
+        l.w = __float_as_uint(w[4 * j + 3] - __uint_as_float(h.w));
+        const int chunk = ((4 * half + j) ^ (m & 7)) << 4;  // 128-byte swizzle
+        *reinterpret_cast<uint4*>(hi + chunk) = h;
+        *reinterpret_cast<uint4*>(lo + chunk) = l;
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       MbarArrive(dequantised(slot));
     }
-    // epilogue: lane = weight row, column = token
+    // epilogue: lane = weight row, column = token; warps w and w + 4 read
+    // the same TMEM lanes (32 (w % 4) ..) and split the tokens
     const bool ok = MbarWait(acc_ready, 0) && !*abort_flag;
     if (!ok && lane == 0) atomicAdd(&g_tc_wait_timeouts, 1u);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const int row = n0 + m;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16);
+    const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < kTileTokens; c += 16) {
+    for (int c = half * (kTileTokens / 2); c < (half + 1) * (kTileTokens / 2); c += 16) {
       uint32_t v[16];
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x16.b32"
@@ -355,7 +408,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int j = 0; j < 16; ++j) {
           const int t = t0 + c + j;
           if (t < t_rows)
-            y[static_cast<int64_t>(t) * n + row] = ok ? __uint_as_float(v[j]) : __int_as_float(0x7fc00000);
+            y[static_cast<int64_t>(t) * n + row] =
+                ok ? __uint_as_float(v[j]) : __int_as_float(0x7fc00000);
         }
       }
     }
@@ -363,13 +417,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // let any load still in flight land before the CTA leaves (only after a
   // timeout can a consumer have stopped early)
   __syncthreads();
-  if (warp == 0 && lane == 0 && *abort_flag) {
+  if (warp == 8 && lane == 0 && *abort_flag) {
     for (int s = issued - S > 0 ? issued - S : 0; s < issued; ++s)
       MbarWait(full(s % S), (s / S) & 1);
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 10) {
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
                  "r"(kTmemColumns)
@@ -377,22 +431,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-// x -> TF32 head and tail, one float4 per thread.
+// x -> TF32 head and exact tail, one float4 per thread.
 __global__ void __launch_bounds__(256)
-    SplitTf32Kernel(const float4* __restrict__ x, float4* __restrict__ xh,
-                    float4* __restrict__ xl, int64_t count4) {
+    SplitTf32Kernel(const float4* __restrict__ x, uint4* __restrict__ xh,
+                    uint4* __restrict__ xl, int64_t count4) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= count4) return;
   const float4 v = x[i];
-  float4 h, l;
-  h.x = Tf32(v.x);
-  h.y = Tf32(v.y);
-  h.z = Tf32(v.z);
-  h.w = Tf32(v.w);
-  l.x = Tf32(v.x - h.x);
-  l.y = Tf32(v.y - h.y);
-  l.z = Tf32(v.z - h.z);
-  l.w = Tf32(v.w - h.w);
+  uint4 h, l;
+  h.x = Tf32Head(__float_as_uint(v.x));
+  h.y = Tf32Head(__float_as_uint(v.y));
+  h.z = Tf32Head(__float_as_uint(v.z));
+  h.w = Tf32Head(__float_as_uint(v.w));
+  l.x = __float_as_uint(v.x - __uint_as_float(h.x));
+  l.y = __float_as_uint(v.y - __uint_as_float(h.y));
+  l.z = __float_as_uint(v.z - __uint_as_float(h.z));
+  l.w = __float_as_uint(v.w - __uint_as_float(h.w));
   xh[i] = h;
   xl[i] = l;
 }
@@ -499,8 +553,8 @@ extern "C" int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t 
   cudaStream_t s = AsStream(stream);
   const int64_t count4 = k * t_rows / 4;
   SplitTf32Kernel<<<static_cast<unsigned>((count4 + 255) / 256), 256, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(xh),
-      reinterpret_cast<float4*>(xl), count4);
+      reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(xh),
+      reinterpret_cast<uint4*>(xl), count4);
   int rc = CheckLaunch("mlb_linear_rows_f32");
   if (rc != MLB_OK) return rc;
   switch (qtype) {
