@@ -19,7 +19,8 @@
 //   - warp 8, one lane: TMA producer.  Per step it loads the raw weight
 //     bytes of the 128 rows (a 2-D uint8 tensor map over [n, row_bytes];
 //     the box starts at the block's byte offset rounded down to 16 and is
-//     64 bytes wide, which covers any 34 / 18 / 20-byte block) and the
+//     64 bytes wide, which covers any 34 / 18 / 20-byte block; 64-byte
+//     swizzle so the per-row reads are bank-conflict free) and the
 //     128 x 32 tiles of xh and xl (fp32 tensor maps, 128-byte swizzle);
 //   - warps 0-7: dequantisers, two threads per weight row (16 values each).
 //     A thread decodes its half of row m's block (byte permutes into the
@@ -188,48 +189,96 @@ __device__ __forceinline__ void BytesToFloats(uint32_t u, float bias, uint64_t& 
                    __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), nb);
 }
 
-__device__ __forceinline__ uint32_t Lds16(const uint8_t* p) {
-  return *reinterpret_cast<const uint16_t*>(p);
+// The raw weight tile holds one 64-byte row per weight row (128 bytes for
+// F32), written by TMA with a 64-byte (128-byte) swizzle: logical 16-byte
+// chunk c of row m sits at chunk c ^ ((m >> 1) & 3) (c ^ (m & 7)).  A
+// thread reads its row with 16-byte loads, which the swizzle spreads over
+// all banks for the 8 rows of a quarter-warp.
+template <int QT>
+__device__ __forceinline__ uint4 RawChunk(const uint8_t* row, int m, int c) {
+  const int phys = QT == MLB_F32 ? (c ^ (m & 7)) : (c ^ ((m >> 1) & 3));
+  return *reinterpret_cast<const uint4*>(row + 16 * phys);
 }
 
-// Half `half` (values 16 * half .. 16 * half + 15) of the block at p, as the
-// reference dequantises them (d * q, d * (n - 8), d * n + m, or the F32
-// value), four values per word of w.
+// Words 0..8 of a block starting at byte `off` of the 16 raw words:
+// out[k] = bytes off + 4k .. off + 4k + 3.
+template <int Q>
+__device__ __forceinline__ void TakeWords(const uint32_t (&w)[16], uint32_t sh,
+                                          uint32_t (&out)[9]) {
+#pragma unroll
+  for (int k = 0; k < 9; ++k) out[k] = __funnelshift_r(w[Q + k], w[Q + k + 1], sh);
+}
+
 template <int QT>
-__device__ __forceinline__ void DequantHalf(const uint8_t* p, int half, float (&w)[16]) {
-  if (QT == MLB_F32) {
-    const float4* f = reinterpret_cast<const float4*>(p + 64 * half);
+__device__ __forceinline__ void DequantBlockHalf(const uint8_t* row, int m, int off, int half,
+                                                 float (&w)[16]);
+
+// Half `half` (values 16 * half .. 16 * half + 15) of row m's block at
+// byte `off` of its raw row, as the reference dequantises them (d * q,
+// d * (n - 8), d * n + m, or the F32 value).
+template <int QT>
+__device__ __forceinline__ void DequantHalf(const uint8_t* row, int m, int off, int half,
+                                            float (&w)[16]) {
+  if constexpr (QT == MLB_F32) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float4 v = f[c];
-      w[4 * c] = v.x;
-      w[4 * c + 1] = v.y;
-      w[4 * c + 2] = v.z;
-      w[4 * c + 3] = v.w;
+      const uint4 v = RawChunk<QT>(row, m, 4 * half + c);
+      w[4 * c] = __uint_as_float(v.x);
+      w[4 * c + 1] = __uint_as_float(v.y);
+      w[4 * c + 2] = __uint_as_float(v.z);
+      w[4 * c + 3] = __uint_as_float(v.w);
     }
-    return;
+  } else {
+    DequantBlockHalf<QT>(row, m, off, half, w);
   }
-  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(Lds16(p))));
+}
+
+template <int QT>
+__device__ __forceinline__ void DequantBlockHalf(const uint8_t* row, int m, int off, int half,
+                                                 float (&w)[16]) {
+  uint32_t raw[16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 v = RawChunk<QT>(row, m, c);
+    raw[4 * c] = v.x;
+    raw[4 * c + 1] = v.y;
+    raw[4 * c + 2] = v.z;
+    raw[4 * c + 3] = v.w;
+  }
+  // the block's first 36 bytes as aligned words (off is the same for the
+  // whole CTA at a given step, so the switch does not diverge)
+  uint32_t blk[9];
+  const uint32_t sh = 8u * (off & 3);
+  switch (off >> 2) {
+    case 0: TakeWords<0>(raw, sh, blk); break;
+    case 1: TakeWords<1>(raw, sh, blk); break;
+    case 2: TakeWords<2>(raw, sh, blk); break;
+    default: TakeWords<3>(raw, sh, blk); break;
+  }
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] & 0xFFFFu)));
   const uint64_t d2 = Pack2(d, d);
   uint32_t words[4];
-  if (QT == MLB_Q8_0) {
-    const uint8_t* q = p + 2 + 16 * half;
+  if (QT == MLB_Q8_0) {  // codes at bytes 2 + 16 * half ..
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      words[i] = (Lds16(q + 4 * i) | (Lds16(q + 4 * i + 2) << 16)) ^ 0x80808080u;
-  } else {
-    const uint8_t* q = p + (QT == MLB_Q4_0 ? 2 : 4);
+    for (int i = 0; i < 4; ++i) {  // (selects, not an indexed load: blk stays in registers)
+      const uint32_t lo = half ? blk[4 + i] : blk[i];
+      const uint32_t hi = half ? blk[5 + i] : blk[1 + i];
+      words[i] = __funnelshift_r(lo, hi, 16) ^ 0x80808080u;
+    }
+  } else if (QT == MLB_Q4_0) {  // nibbles at bytes 2 .. 17
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t u = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(q + 4 * i)
-                                        : (Lds16(q + 4 * i) | (Lds16(q + 4 * i + 2) << 16));
+      const uint32_t u = __funnelshift_r(blk[i], blk[i + 1], 16);
       words[i] = (half ? u >> 4 : u) & 0x0F0F0F0Fu;
     }
+  } else {  // Q4_1: nibbles at bytes 4 .. 19
+#pragma unroll
+    for (int i = 0; i < 4; ++i) words[i] = (half ? blk[1 + i] >> 4 : blk[1 + i]) & 0x0F0F0F0Fu;
   }
   const float bias = QT == MLB_Q8_0 ? 8388736.0f : (QT == MLB_Q4_0 ? 8388616.0f : 8388608.0f);
-  const float mn = QT == MLB_Q4_1
-                       ? __half2float(__ushort_as_half(static_cast<unsigned short>(Lds16(p + 2))))
-                       : 0.0f;
+  const float mn =
+      QT == MLB_Q4_1 ? __half2float(__ushort_as_half(static_cast<unsigned short>(blk[0] >> 16)))
+                     : 0.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     uint64_t a, b;
@@ -364,7 +413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       float w[16];
-      DequantHalf<QT>(raw + slot * kTileRows * kRaw + m * kRaw + ((s * kBB) & 15), half, w);
+      DequantHalf<QT>(raw + slot * kTileRows * kRaw + m * kRaw, m, (s * kBB) & 15, half, w);
       uint8_t* hi = base + (a_hi(slot) - sbase) + m * 128;
       uint8_t* lo = base + (a_lo(slot) - sbase) + m * 128;
 #pragma unroll
@@ -486,7 +535,8 @@ int LaunchTc(const void* w, int64_t n, int64_t k, int64_t row_bytes, const float
   CUtensorMap wmap, xhmap, xlmap;
   if (!Map2D(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(row_bytes),
              static_cast<uint64_t>(n), static_cast<uint64_t>(row_bytes), TcRawBytes(QT),
-             kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+             kTileRows,
+             QT == MLB_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
       !Map2D(&xhmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xh, static_cast<uint64_t>(k),
              static_cast<uint64_t>(t_rows), static_cast<uint64_t>(k) * 4, kStepK, kTileTokens,
              CU_TENSOR_MAP_SWIZZLE_128B) ||
