@@ -26,17 +26,20 @@
 //     A thread decodes its half of row m's block (byte permutes into the
 //     mantissa of 2^23 instead of int->float conversions, packed f32x2
 //     arithmetic), splits each value into its TF32 head (the top 19 bits,
-//     a mask) and the exact remainder, and writes both into 128 x 32 tiles
-//     in the K-major 128-byte-swizzled layout the MMA reads;
+//     a mask) and the exact remainder, and stores both straight into tensor
+//     memory (tcgen05.st; row m is lane m, one value per column) — the MMA
+//     reads its A operand from there, so shared memory only carries the
+//     raw weights and the x tiles;
 //   - warp 9, one lane: MMA issuer.  Per step 4 k-slices x 3 products of
-//     tcgen05.mma.cta_group::1.kind::tf32 (M = 128, N = 128, K = 8) into a
-//     128-column fp32 accumulator in tensor memory; tcgen05.commit frees the
-//     stage's buffers;
+//     tcgen05.mma.cta_group::1.kind::tf32 (M = 128, N = 128, K = 8; A from
+//     tensor memory, B from shared memory) into a 128-column fp32
+//     accumulator in tensor memory; tcgen05.commit frees the stage's
+//     buffers;
 //   - warp 10 allocates / frees the tensor memory; warps 0-7 finally read
 //     the accumulator (tcgen05.ld, lane = weight row; warps w and w + 4
 //     share TMEM lanes 32w.. and take one half of the tokens each) and store
 //     y[t, row], 32 consecutive rows per warp store.
-// Stages form a ring (3 for the quantised formats, 2 for F32) tracked by
+// Stages form a ring (5 for the quantised formats, 4 for F32) tracked by
 // mbarriers; every wait is bounded (a wait that gives up is counted in
 // g_tc_wait_timeouts and the CTA writes NaN instead of its tile).
 // x is split into xh / xl by a small kernel first (caller scratch).
@@ -60,19 +63,21 @@ constexpr int kStepK = 32;        // k per stage: one ggml block
 constexpr int kTcThreads = 352;       // 8 dequant/epilogue warps + producer, MMA, TMEM
 constexpr int kDequantThreads = 256;  // two per weight row
 constexpr int kTileBytes = kTileRows * kStepK * 4;  // one 128 x 32 fp32 tile
-constexpr int kTmemColumns = 128;
+constexpr int kTmemColumns = 512;  // accumulator (128) + the A ring (64 per stage)
+constexpr int kAccColumns = kTileTokens;
+constexpr int kATileColumns = kStepK;  // one TF32 per column, row m in lane m
 
 __host__ __device__ constexpr int TcBlockBytes(int qt) {
   return qt == MLB_F32 ? 128 : (qt == MLB_Q8_0 ? 34 : (qt == MLB_Q4_0 ? 18 : 20));
 }
 __host__ __device__ constexpr int TcRawBytes(int qt) { return qt == MLB_F32 ? 128 : 64; }
-__host__ __device__ constexpr int TcStages(int qt) { return qt == MLB_F32 ? 2 : 3; }
+__host__ __device__ constexpr int TcStages(int qt) { return qt == MLB_F32 ? 4 : 5; }
 
-// Shared-memory layout from a 1024-byte aligned base: per stage four tiles
-// (A head, A tail, B head, B tail), then the raw weight tiles, then the
-// mbarriers (full, dequantised, empty per stage; accumulator ready) and the
-// tensor-memory address.
-__host__ __device__ constexpr int TcRawOffset(int qt) { return TcStages(qt) * 4 * kTileBytes; }
+// Shared-memory layout from a 1024-byte aligned base: per stage two tiles
+// (B head, B tail), then the raw weight tiles, then the mbarriers (full,
+// dequantised, empty per stage; accumulator ready) and the tensor-memory
+// address.  The A tiles live in tensor memory.
+__host__ __device__ constexpr int TcRawOffset(int qt) { return TcStages(qt) * 2 * kTileBytes; }
 __host__ __device__ constexpr int TcBarOffset(int qt) {
   return TcRawOffset(qt) + TcStages(qt) * kTileRows * TcRawBytes(qt);
 }
@@ -138,12 +143,23 @@ constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) |
                                 (static_cast<uint32_t>(kTileTokens >> 3) << 17) |
                                 (static_cast<uint32_t>(kTileRows >> 4) << 24);
 
-__device__ __forceinline__ void MmaTf32(uint32_t tmem, uint64_t a, uint64_t b,
+// D[tmem] (+)= A[a_tmem] . B[b_desc]^T, A read from tensor memory (row m in
+// lane m, one TF32 per column), B from shared memory.
+__device__ __forceinline__ void MmaTf32(uint32_t tmem, uint32_t a_tmem, uint64_t b,
                                         uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(a), "l"(b), "r"(kInstrDesc), "r"(accumulate)
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+      "r"(a_tmem), "l"(b), "r"(kInstrDesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void TmemStore16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
       : "memory");
 }
 __device__ __forceinline__ void MmaCommit(uint32_t bar) {
@@ -319,10 +335,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t raw_addr = SmemU32(smem_raw);
   uint8_t* base = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sbase = SmemU32(base);
-  auto a_hi = [&](int s) { return sbase + s * 4 * kTileBytes; };
-  auto a_lo = [&](int s) { return sbase + s * 4 * kTileBytes + kTileBytes; };
-  auto b_hi = [&](int s) { return sbase + s * 4 * kTileBytes + 2 * kTileBytes; };
-  auto b_lo = [&](int s) { return sbase + s * 4 * kTileBytes + 3 * kTileBytes; };
+  auto b_hi = [&](int s) { return sbase + s * 2 * kTileBytes; };
+  auto b_lo = [&](int s) { return sbase + s * 2 * kTileBytes + kTileBytes; };
+  // tensor-memory columns of stage s's A head and tail tiles
+  auto a_hi_col = [&](int s) { return kAccColumns + s * 2 * kATileColumns; };
+  auto a_lo_col = [&](int s) { return kAccColumns + s * 2 * kATileColumns + kATileColumns; };
   uint8_t* raw = base + TcRawOffset(QT);
   const uint32_t bars = sbase + TcBarOffset(QT);
   auto full = [&](int s) { return bars + 8 * s; };
@@ -390,8 +407,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
 #pragma unroll
         for (int j = 0; j < kStepK / 8; ++j) {  // K = 8 TF32 = 32 bytes per MMA
-          const uint64_t ah = SmemDesc(a_hi(slot) + 32 * j);
-          const uint64_t al = SmemDesc(a_lo(slot) + 32 * j);
+          const uint32_t ah = tmem + a_hi_col(slot) + 8 * j;
+          const uint32_t al = tmem + a_lo_col(slot) + 8 * j;
           const uint64_t bh = SmemDesc(b_hi(slot) + 32 * j);
           const uint64_t bl = SmemDesc(b_lo(slot) + 32 * j);
           MmaTf32(tmem, ah, bh, (s | j) != 0 ? 1u : 0u);
@@ -414,24 +431,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       float w[16];
       DequantHalf<QT>(raw + slot * kTileRows * kRaw + m * kRaw, m, (s * kBB) & 15, half, w);
-      uint8_t* hi = base + (a_hi(slot) - sbase) + m * 128;
-      uint8_t* lo = base + (a_lo(slot) - sbase) + m * 128;
+      uint32_t h[16], l[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 h, l;
-        h.x = Tf32Head(__float_as_uint(w[4 * j]));
-        h.y = Tf32Head(__float_as_uint(w[4 * j + 1]));
-        h.z = Tf32Head(__float_as_uint(w[4 * j + 2]));
-        h.w = Tf32Head(__float_as_uint(w[4 * j + 3]));
-        l.x = __float_as_uint(w[4 * j] - __uint_as_float(h.x));
-        l.y = __float_as_uint(w[4 * j + 1] - __uint_as_float(h.y));
-        l.z = __float_as_uint(w[4 * j + 2] - __uint_as_float(h.z));
-        l.w = __float_as_uint(w[4 * j + 3] - __uint_as_float(h.w));
-        const int chunk = ((4 * half + j) ^ (m & 7)) << 4;  // 128-byte swizzle
-        *reinterpret_cast<uint4*>(hi + chunk) = h;
-        *reinterpret_cast<uint4*>(lo + chunk) = l;
+      for (int i = 0; i < 16; ++i) {
+        h[i] = Tf32Head(__float_as_uint(w[i]));
+        l[i] = __float_as_uint(w[i] - __uint_as_float(h[i]));
       }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      // (the MMAs that last read this slot's A tiles finished before its
+      // loads were issued; order the stores after that)
+      asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+      // this warp's 32 lanes (rows), 16 columns each for its half of the block
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+      TmemStore16(lane_base + a_hi_col(slot) + 16 * half, h);
+      TmemStore16(lane_base + a_lo_col(slot) + 16 * half, l);
+      asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
       MbarArrive(dequantised(slot));
     }
     // epilogue: lane = weight row, column = token; warps w and w + 4 read
