@@ -251,6 +251,265 @@ int ValidateAttention(const float* q, const float* keys, const float* values,
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Prompt chunks: tiles of query rows.
+//
+// CTA (kv head g, tile of QR = 64 / G consecutive query rows) holds the
+// QV = QR * G query vectors of its rows and group in shared memory and walks
+// the visible positions in blocks of 32 keys: every K/V block is staged once
+// (cp.async, double-buffered) for all QV query vectors instead of once per
+// query row.  256 threads; thread (pair p = tid / 8, j = tid % 8) scores
+// query vectors 2p, 2p + 1 against keys j, j + 8, j + 16, j + 24 of a block
+// (rows padded by 16 bytes so those reads hit distinct banks), keeps the
+// online softmax of its two vectors (max / sum reduced over the 8 threads of
+// the pair) and accumulates P.V for float4 columns j, j + 8, ... of them.
+// Masked (future) keys score -inf; no slice partials, no combine kernel.
+constexpr int kTileKeys = 32;
+constexpr int kTileQv = 64;
+constexpr int kTileThreads = 256;
+
+struct AttnTileArgs {
+  const float* q;
+  const float* keys;
+  const float* values;
+  float* out;
+  int64_t position;  // query row r is the token at position + r
+  int64_t rows;
+  int64_t max_seq;
+  int n_heads;
+  int n_kv_heads;
+  float scale;
+};
+
+template <int HD4>
+__host__ __device__ constexpr int TileRowFloats() { return 4 * HD4 + 4; }  // one padded row
+
+template <int G, int HD4>
+constexpr size_t TileSmemBytes() {
+  return sizeof(float) * (static_cast<size_t>(kTileQv + 4 * kTileKeys) * TileRowFloats<HD4>() +
+                          static_cast<size_t>(kTileQv) * (kTileKeys + 1));
+}
+
+template <int G, int HD4>
+__global__ void __launch_bounds__(kTileThreads) AttnRowTileKernel(AttnTileArgs a) {
+  constexpr int QR = kTileQv / G;  // query rows per CTA
+  constexpr int QV = QR * G;
+  constexpr int RF = TileRowFloats<HD4>();
+  constexpr int HD = 4 * HD4;
+  constexpr int CPT = HD4 / 8;     // float4 columns per thread in P.V
+  extern __shared__ __align__(16) float tsm[];
+  float* qs = tsm;                           // [QV][RF]
+  float* ks = qs + kTileQv * RF;             // [2][kTileKeys][RF]
+  float* vs = ks + 2 * kTileKeys * RF;       // [2][kTileKeys][RF]
+  float* ps = vs + 2 * kTileKeys * RF;       // [QV][kTileKeys + 1]
+
+  const int g = blockIdx.x;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * QR;
+  const int tid = threadIdx.x;
+  const int pair = tid >> 3;
+  const int j = tid & 7;
+  const int v0 = 2 * pair, v1 = 2 * pair + 1;
+  const bool active = v1 < QV;  // (QV is even: both or neither)
+  const int64_t row_stride = static_cast<int64_t>(a.n_heads) * HD;
+  const int64_t kv_stride = static_cast<int64_t>(a.n_kv_heads) * HD;
+
+  // the tile's query vectors (rows beyond the chunk read as zeros)
+  for (int i = tid; i < QV * HD4; i += kTileThreads) {
+    const int v = i / HD4, d4 = i - v * HD4;
+    const int64_t row = r0 + v / G;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < a.rows)
+      x = *reinterpret_cast<const float4*>(a.q + row * row_stride +
+                                           static_cast<int64_t>(g * G + v % G) * HD + 4 * d4);
+    *reinterpret_cast<float4*>(qs + v * RF + 4 * d4) = x;
+  }
+  const int64_t last_row = r0 + QR - 1 < a.rows - 1 ? r0 + QR - 1 : a.rows - 1;
+  const int64_t visible = a.position + last_row + 1;  // keys any row of the tile sees
+  const int blocks = static_cast<int>((visible + kTileKeys - 1) / kTileKeys);
+
+  auto stage = [&](int b) {
+    float* kd = ks + (b & 1) * kTileKeys * RF;
+    float* vd = vs + (b & 1) * kTileKeys * RF;
+    for (int i = tid; i < kTileKeys * HD4; i += kTileThreads) {
+      const int key = i / HD4, d4 = i - key * HD4;
+      const int64_t t = static_cast<int64_t>(b) * kTileKeys + key;
+      if (t < a.max_seq) {
+        const int64_t off = t * kv_stride + static_cast<int64_t>(g) * HD + 4 * d4;
+        CopyAsync16(kd + key * RF + 4 * d4, a.keys + off);
+        CopyAsync16(vd + key * RF + 4 * d4, a.values + off);
+      }
+    }
+  };
+
+  const int64_t qpos0 = a.position + r0 + v0 / G;  // positions of the two vectors
+  const int64_t qpos1 = a.position + r0 + v1 / G;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  float4 acc0[CPT], acc1[CPT];
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    acc0[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    acc1[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  stage(0);
+  CopyAsyncCommit();
+  for (int b = 0; b < blocks; ++b) {
+    if (b + 1 < blocks) stage(b + 1);
+    CopyAsyncCommit();
+    CopyAsyncWait<1>();
+    __syncthreads();  // block b (and, on b == 0, the query tile) in place
+    const float* kb = ks + (b & 1) * kTileKeys * RF;
+    const float* vb = vs + (b & 1) * kTileKeys * RF;
+    if (active) {
+      float s0[4], s1[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s0[i] = s1[i] = 0.0f;
+#pragma unroll 4
+      for (int d4 = 0; d4 < HD4; ++d4) {
+        const float4 qa = *reinterpret_cast<const float4*>(qs + v0 * RF + 4 * d4);
+        const float4 qb = *reinterpret_cast<const float4*>(qs + v1 * RF + 4 * d4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 kk = *reinterpret_cast<const float4*>(kb + (j + 8 * i) * RF + 4 * d4);
+          s0[i] = fmaf(qa.x, kk.x, s0[i]);
+          s0[i] = fmaf(qa.y, kk.y, s0[i]);
+          s0[i] = fmaf(qa.z, kk.z, s0[i]);
+          s0[i] = fmaf(qa.w, kk.w, s0[i]);
+          s1[i] = fmaf(qb.x, kk.x, s1[i]);
+          s1[i] = fmaf(qb.y, kk.y, s1[i]);
+          s1[i] = fmaf(qb.z, kk.z, s1[i]);
+          s1[i] = fmaf(qb.w, kk.w, s1[i]);
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t t = static_cast<int64_t>(b) * kTileKeys + j + 8 * i;
+        s0[i] = t <= qpos0 ? __fmul_rn(s0[i], a.scale) : -INFINITY;
+        s1[i] = t <= qpos1 ? __fmul_rn(s1[i], a.scale) : -INFINITY;
+        mx0 = fmaxf(mx0, s0[i]);
+        mx1 = fmaxf(mx1, s1[i]);
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      // a vector with no visible key yet keeps p = 0 (no -inf - -inf)
+      const float al0 = n0 == -INFINITY ? 1.0f : expf(m0 - n0);
+      const float al1 = n1 == -INFINITY ? 1.0f : expf(m1 - n1);
+      float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float p0 = s0[i] == -INFINITY ? 0.0f : expf(s0[i] - n0);
+        const float p1 = s1[i] == -INFINITY ? 0.0f : expf(s1[i] - n1);
+        ps[v0 * (kTileKeys + 1) + j + 8 * i] = p0;
+        ps[v1 * (kTileKeys + 1) + j + 8 * i] = p1;
+        sum0 += p0;
+        sum1 += p1;
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, o);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
+      }
+      l0 = fmaf(l0, al0, sum0);
+      l1 = fmaf(l1, al1, sum1);
+      m0 = n0;
+      m1 = n1;
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        acc0[c].x *= al0; acc0[c].y *= al0; acc0[c].z *= al0; acc0[c].w *= al0;
+        acc1[c].x *= al1; acc1[c].y *= al1; acc1[c].z *= al1; acc1[c].w *= al1;
+      }
+      __syncwarp();  // the pair's p values are in place (the 8 threads share a warp)
+#pragma unroll 4
+      for (int key = 0; key < kTileKeys; ++key) {
+        const float p0 = ps[v0 * (kTileKeys + 1) + key];
+        const float p1 = ps[v1 * (kTileKeys + 1) + key];
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          const float4 vv = *reinterpret_cast<const float4*>(vb + key * RF + 4 * (j + 8 * c));
+          acc0[c].x = fmaf(p0, vv.x, acc0[c].x);
+          acc0[c].y = fmaf(p0, vv.y, acc0[c].y);
+          acc0[c].z = fmaf(p0, vv.z, acc0[c].z);
+          acc0[c].w = fmaf(p0, vv.w, acc0[c].w);
+          acc1[c].x = fmaf(p1, vv.x, acc1[c].x);
+          acc1[c].y = fmaf(p1, vv.y, acc1[c].y);
+          acc1[c].z = fmaf(p1, vv.z, acc1[c].z);
+          acc1[c].w = fmaf(p1, vv.w, acc1[c].w);
+        }
+      }
+    }
+    __syncthreads();  // buffers of block b are free for block b + 2
+  }
+  CopyAsyncWait<0>();
+  if (!active) return;
+  const int64_t row0 = r0 + v0 / G, row1 = r0 + v1 / G;
+  float* o0 = a.out + row0 * row_stride + static_cast<int64_t>(g * G + v0 % G) * HD;
+  float* o1 = a.out + row1 * row_stride + static_cast<int64_t>(g * G + v1 % G) * HD;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    const int col = 4 * (j + 8 * c);
+    if (row0 < a.rows)
+      *reinterpret_cast<float4*>(o0 + col) =
+          make_float4(__fdiv_rn(acc0[c].x, l0), __fdiv_rn(acc0[c].y, l0),
+                      __fdiv_rn(acc0[c].z, l0), __fdiv_rn(acc0[c].w, l0));
+    if (row1 < a.rows)
+      *reinterpret_cast<float4*>(o1 + col) =
+          make_float4(__fdiv_rn(acc1[c].x, l1), __fdiv_rn(acc1[c].y, l1),
+                      __fdiv_rn(acc1[c].z, l1), __fdiv_rn(acc1[c].w, l1));
+  }
+}
+
+template <int G, int HD4>
+int LaunchRowTile(const AttnTileArgs& a, cudaStream_t s) {
+  constexpr int QR = kTileQv / G;
+  constexpr size_t shm = TileSmemBytes<G, HD4>();
+  auto kernel = AttnRowTileKernel<G, HD4>;
+  if (shm > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(shm)) != cudaSuccess) {
+    cudaGetLastError();
+    return Fail(MLB_ERR_CUDA, "attention: shared memory opt-in");
+  }
+  const dim3 grid(static_cast<unsigned>(a.n_kv_heads),
+                  static_cast<unsigned>((a.rows + QR - 1) / QR));
+  kernel<<<grid, kTileThreads, shm, s>>>(a);
+  return CheckLaunch("attention (row tiles)");
+}
+
+// Row tiles when they fill the GPU (n_kv_heads x row tiles >= half the SMs),
+// group 1 / 2 / 4 / 8, head_dim 64 or 128; -1 when the shape does not fit.
+int AttentionRowTiles(const float* q, const float* keys, const float* values, float* out,
+                      int64_t position, int64_t rows, int64_t max_seq, int n_heads,
+                      int n_kv_heads, int hd, cudaStream_t s) {
+  const int group = n_heads / n_kv_heads;
+  if ((group != 1 && group != 2 && group != 4 && group != 8) || (hd != 64 && hd != 128) ||
+      !Aligned16(out) || rows > 65535LL * (kTileQv / group))
+    return -1;
+  if (static_cast<int64_t>(n_kv_heads) * ((rows + kTileQv / group - 1) / (kTileQv / group)) <
+      SmCount() / 2)
+    return -1;
+  AttnTileArgs a{q, keys, values, out, position, rows, max_seq, n_heads, n_kv_heads,
+                 1.0f / std::sqrt(static_cast<float>(hd))};
+  if (hd == 64) {
+    switch (group) {
+      case 1: return LaunchRowTile<1, 16>(a, s);
+      case 2: return LaunchRowTile<2, 16>(a, s);
+      case 4: return LaunchRowTile<4, 16>(a, s);
+      default: return LaunchRowTile<8, 16>(a, s);
+    }
+  }
+  switch (group) {
+    case 1: return LaunchRowTile<1, 32>(a, s);
+    case 2: return LaunchRowTile<2, 32>(a, s);
+    case 4: return LaunchRowTile<4, 32>(a, s);
+    default: return LaunchRowTile<8, 32>(a, s);
+  }
+}
+
 // Shared by the entry points: scratch must hold AttentionScratchFloats() for
 // `rows` query rows, row r seeing visible + r positions.
 int64_t AttentionScratchFloats(int n_heads, int n_kv_heads, int hd, int64_t visible,
@@ -268,6 +527,12 @@ int AttentionRows(const float* q, const float* keys, const float* values, float*
   if (rc != MLB_OK) return rc;
   if (rows < 1 || position + rows > max_seq)
     return Fail(MLB_ERR_RANGE, "attention: rows leave the cache");
+  cudaStream_t s = AsStream(stream);
+  if (rows > 1) {
+    rc = AttentionRowTiles(q, keys, values, out, position, rows, max_seq, n_heads,
+                           n_kv_heads, hd, s);
+    if (rc >= 0) return rc;  // -1: shape not covered, use the split form
+  }
   AttnArgs a{};
   a.keys = keys;
   a.values = values;
@@ -280,7 +545,6 @@ int AttentionRows(const float* q, const float* keys, const float* values, float*
   // 1 / std::sqrt((float)head_dim) as the reference computes it (forward.cc:75)
   a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
   const int nv = (hd / 4 + 31) / 32;
-  cudaStream_t s = AsStream(stream);
   const int64_t per_row = static_cast<int64_t>(n_heads) * hd;
   constexpr int64_t kMaxRowsPerLaunch = 65535;  // grid.z
   for (int64_t r0 = 0; r0 < rows; r0 += kMaxRowsPerLaunch) {

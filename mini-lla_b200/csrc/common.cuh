@@ -109,4 +109,18 @@ __device__ __forceinline__ float BlockMax(float v, float* scratch) {
   return WarpMax(t);
 }
 
+// 16-byte global -> shared copies that bypass registers (cp.async).
+__device__ __forceinline__ void CopyAsync16(void* smem_dst, const void* gmem_src) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst),
+               "l"(gmem_src));
+}
+__device__ __forceinline__ void CopyAsyncCommit() {
+  asm volatile("cp.async.commit_group;\n" ::);
+}
+template <int N>
+__device__ __forceinline__ void CopyAsyncWait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
 }  // namespace mlb

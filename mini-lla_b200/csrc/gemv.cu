@@ -94,21 +94,6 @@ __device__ __forceinline__ float Dot4(const float4& a, const float4& b, float ac
   return fmaf(a.w, b.w, acc);
 }
 
-// 16-byte global -> shared copies that bypass registers (cp.async), so a
-// lane keeps every copy of a chunk in flight at once.
-__device__ __forceinline__ void CopyAsync16(void* smem_dst, const void* gmem_src) {
-  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst),
-               "l"(gmem_src));
-}
-__device__ __forceinline__ void CopyAsyncCommit() {
-  asm volatile("cp.async.commit_group;\n" ::);
-}
-template <int N>
-__device__ __forceinline__ void CopyAsyncWait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
 // Dynamic shared memory holds two stages; a stage is the x chunk
 // [T][kChunk] floats followed by one weight slice of `slice` bytes per warp.
 // Chunk c + 1 is copied in (cp.async) while chunk c is computed.

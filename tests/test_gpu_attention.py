@@ -136,3 +136,32 @@ def test_attention_rows_rejects_rows_beyond_cache(cuda):
 def torch_zeros(shape, device):
     import torch
     return torch.zeros(shape, dtype=torch.float32, device=device)
+
+
+@pytest.mark.parametrize("nh,nkv,hd,pos,rows,max_seq", [
+    (32, 8, 128, 0, 512, 600),      # group 4, a prompt from position 0
+    (32, 32, 128, 100, 300, 512),   # group 1, partial last tile
+    (16, 2, 64, 7, 1000, 1100),     # group 8, head_dim 64
+    (64, 32, 128, 1500, 100, 1700), # group 2, chunk after a long context
+    (32, 8, 64, 33, 333, 400)])     # head_dim 64, ragged everything
+def test_attention_row_tiles_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max_seq):
+    """Prompt chunks large enough for the query-row tile kernel (n_kv_heads x
+    row tiles >= half the SMs): sampled rows (first, last, tile edges, random)
+    against per-position decode attention of the oracle."""
+    import torch
+    rng = np.random.default_rng(rows + pos)
+    q = rng.standard_normal((rows, nh, hd), dtype=np.float32)
+    keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    values = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    got = mlb.attention_rows(dev(q, cuda), dev(keys, cuda), dev(values, cuda), pos)
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    qr = 64 // (nh // nkv)
+    sample = {0, 1, rows - 1, rows - 2, qr - 1, qr, min(rows - 1, 2 * qr + 1)}
+    sample |= set(rng.integers(0, rows, 6).tolist())
+    for r in sorted(sample):
+        want = oracle.attention_decode(q[r], keys, values, pos + r, nh, nkv)
+        mag = _magnitude(q[r], keys, values, pos + r, nh, nkv)
+        err = np.abs(got[r].astype(np.float64) - want)
+        ratio = float((err / np.maximum(mag, 1e-30)).max())
+        assert ratio <= 1e-5, f"row {r}: max error / magnitude {ratio:.2e}"
