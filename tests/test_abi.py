@@ -73,6 +73,23 @@ def test_bad_arguments_rejected_on_host():
         lambda: lib.mlb_embedding_gather(ctypes.c_void_p(17), 1, 4, 32, bogus, 1,
                                          bogus, None, None),
         lambda: lib.mlb_status_check(None, None, None),
+        # linear layers: unknown format, negative sizes, missing scratch for
+        # a prompt-sized batch
+        lambda: lib.mlb_linear_f32(bogus, 9, 4, 32, bogus, 1, bogus, None),
+        lambda: lib.mlb_linear_f32(bogus, 1, -4, 32, bogus, 1, bogus, None),
+        lambda: lib.mlb_linear_rows_f32(bogus, 9, 4, 32, bogus, 64, bogus, bogus, 1 << 20,
+                                        None),
+        lambda: lib.mlb_linear_rows_f32(ctypes.c_void_p(64), 1, 128, 256,
+                                        ctypes.c_void_p(64), 64, bogus, None, 0, None),
+        # attention: group not dividing, null scratch, rows < 0
+        lambda: lib.mlb_attention_decode_f32(bogus, bogus, bogus, bogus, 3, 8, 6, 4, 64,
+                                             bogus, 1 << 20, None),
+        lambda: lib.mlb_attention_rows_f32(bogus, bogus, bogus, bogus, 0, 4, 8, 8, 2, 64,
+                                           None, 0, None),
+        lambda: lib.mlb_attention_rows_f32(bogus, bogus, bogus, bogus, 0, -1, 8, 8, 2, 64,
+                                           bogus, 1 << 20, None),
+        lambda: lib.mlb_kv_write_f32(None, bogus, bogus, bogus, 0, 1, 8, 2, 64, None),
+        lambda: lib.mlb_wait_timeouts(None),
     ]
     for i, call in enumerate(cases):
         assert call() == 1, f"case {i} not rejected"
