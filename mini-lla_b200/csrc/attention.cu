@@ -209,11 +209,184 @@ __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
   }
 }
 
+// Lane-per-position form of the slice kernel (head_dim 64 or 128): each
+// warp takes its slice's positions 32 at a time, stages those 32 K rows in
+// shared memory (cp.async, rows padded by 16 bytes so that a lane reading
+// its own row stays on distinct banks), and lane l scores position
+// block + l against all G query heads with plain FMAs — no cross-lane
+// reduction per dot product.  One warp max / sum per block and head feeds
+// the online softmax; P.V then walks the block's positions with the
+// probabilities broadcast by shuffles and each lane accumulating DPL = hd / 32
+// dimensions of a coalesced V row.  The 4 warps' states are merged and
+// written as the slice partial, as in AttnPartialKernel.
+constexpr int kLaneBlock = 32;
+
+template <int HD4>
+__host__ __device__ constexpr int LaneRowFloats() { return 4 * HD4 + 4; }
+
+template <int G, int HD4>
+__global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArgs a) {
+  constexpr int HD = 4 * HD4;
+  constexpr int DPL = HD / 32;        // dimensions per lane in P.V (2 or 4)
+  constexpr int RF = LaneRowFloats<HD4>();
+  // dynamic: q of the G heads, then per warp a staged block of K rows (the
+  // warps' final accumulators reuse the K area once the loop is done)
+  extern __shared__ __align__(16) float lsm[];
+  float* qs = lsm;                   // [G][HD]
+  float* ks_all = lsm + G * HD;      // [kAttnWarps][kLaneBlock][RF]
+  __shared__ float sm_m[kAttnWarps][G];
+  __shared__ float sm_l[kAttnWarps][G];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int g = blockIdx.x;
+  const int s = blockIdx.y;
+  const int64_t row = blockIdx.z;
+  const int64_t t_begin = s * a.slice;
+  const int64_t t_end = min(a.visible + row, t_begin + a.slice);
+  const float* q_row = a.q + row * a.n_heads * HD;
+  float* scratch_row = a.scratch + row * a.n_heads * a.splits * (HD + 2);
+  const int64_t kv_stride = static_cast<int64_t>(a.n_kv_heads) * HD;
+  const float* kbase = a.keys + static_cast<int64_t>(g) * HD;
+  const float* vbase = a.values + static_cast<int64_t>(g) * HD;
+
+  for (int i = threadIdx.x; i < G * HD4; i += blockDim.x)
+    reinterpret_cast<float4*>(qs)[i] =
+        __ldg(reinterpret_cast<const float4*>(q_row + static_cast<int64_t>(g) * G * HD) + i);
+  __syncthreads();
+
+  float m[G], l[G], acc[G][DPL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[h][e] = 0.0f;
+  }
+  float* kw = ks_all + warp * kLaneBlock * RF;
+  for (int64_t blk = t_begin + static_cast<int64_t>(warp) * kLaneBlock; blk < t_end;
+       blk += kAttnWarps * kLaneBlock) {
+    const int n = static_cast<int>(t_end - blk < kLaneBlock ? t_end - blk : kLaneBlock);
+    // stage K rows blk .. blk + n - 1 (coalesced: lane l copies float4 l, l + 32, ...)
+    for (int i = lane; i < n * HD4; i += 32) {
+      const int r = i / HD4, c = i - r * HD4;
+      CopyAsync16(kw + r * RF + 4 * c, kbase + (blk + r) * kv_stride + 4 * c);
+    }
+    CopyAsyncCommit();
+    CopyAsyncWait<0>();
+    __syncwarp();
+    // scores of position blk + lane for the G heads
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+    if (lane < n) {
+      const float* kr = kw + lane * RF;
+#pragma unroll 8
+      for (int c = 0; c < HD4; ++c) {
+        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * c);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + h * HD + 4 * c);
+          sc[h] = fmaf(qv.x, kv.x, sc[h]);
+          sc[h] = fmaf(qv.y, kv.y, sc[h]);
+          sc[h] = fmaf(qv.z, kv.z, sc[h]);
+          sc[h] = fmaf(qv.w, kv.w, sc[h]);
+        }
+      }
+    }
+    float p[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float score = lane < n ? __fmul_rn(sc[h], a.scale) : -INFINITY;
+      const float m_new = fmaxf(m[h], WarpMax(score));
+      const float alpha = expf(m[h] - m_new);  // 0 on the first block
+      p[h] = lane < n ? expf(score - m_new) : 0.0f;
+      l[h] = fmaf(l[h], alpha, WarpSum(p[h]));
+      m[h] = m_new;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) acc[h][e] *= alpha;
+    }
+    // P.V over the block's positions (V row r: lane owns dims DPL * lane ..)
+    for (int r = 0; r < n; ++r) {
+      const float* vr = vbase + (blk + r) * kv_stride + DPL * lane;
+      float v[DPL];
+      if (DPL == 4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(vr));
+        v[0] = x.x; v[1] = x.y; v[2 % DPL] = x.z; v[3 % DPL] = x.w;
+      } else {
+        const float2 x = __ldg(reinterpret_cast<const float2*>(vr));
+        v[0] = x.x; v[1] = x.y;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float pr = __shfl_sync(0xffffffffu, p[h], r);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(pr, v[e], acc[h][e]);
+      }
+    }
+    __syncwarp();  // every lane is done with kw before it is restaged
+  }
+  // merge the 4 warps, then write the slice partial
+  __syncthreads();  // every warp is done with its K rows: reuse them
+  float* sm_acc = ks_all;  // [kAttnWarps][G][HD]
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    if (lane == 0) {
+      sm_m[warp][h] = m[h];
+      sm_l[warp][h] = l[h];
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) sm_acc[(warp * G + h) * HD + DPL * lane + e] = acc[h][e];
+  }
+  __syncthreads();
+  for (int h = warp; h < G; h += kAttnWarps) {
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm_m[w][h]);
+    float ll = 0.0f, aa[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) aa[e] = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = sm_m[w][h] == -INFINITY ? 0.0f : expf(sm_m[w][h] - mm);
+      ll = fmaf(sm_l[w][h], f, ll);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) aa[e] = fmaf(sm_acc[(w * G + h) * HD + DPL * lane + e], f, aa[e]);
+    }
+    float* part = scratch_row + (static_cast<int64_t>(g * G + h) * a.splits + s) * (HD + 2);
+    if (lane == 0) {
+      part[0] = mm;
+      part[1] = ll;
+    }
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) part[2 + DPL * lane + e] = aa[e];
+  }
+}
+
+template <int G, int HD4>
+int LaunchLane(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+  constexpr size_t kStage = static_cast<size_t>(kAttnWarps) * kLaneBlock * LaneRowFloats<HD4>();
+  constexpr size_t kAcc = static_cast<size_t>(kAttnWarps) * G * 4 * HD4;
+  constexpr size_t shm = sizeof(float) * (G * 4 * HD4 + (kStage > kAcc ? kStage : kAcc));
+  auto kernel = AttnLanePartialKernel<G, HD4>;
+  if (shm > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(shm)) != cudaSuccess) {
+    cudaGetLastError();
+    return Fail(MLB_ERR_CUDA, "attention: shared memory opt-in");
+  }
+  kernel<<<grid, kAttnWarps * 32, shm, s>>>(a);
+  return CheckLaunch("mlb_attention_decode_f32");
+}
+
 template <int G>
 int LaunchPartial(const AttnArgs& a, int64_t rows, int nv, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(a.n_kv_heads), static_cast<unsigned>(a.splits),
                   static_cast<unsigned>(rows));
-  if (nv == 1) {
+  if (a.hd == 128) {
+    return LaunchLane<G, 32>(a, grid, s);
+  } else if (a.hd == 64) {
+    return LaunchLane<G, 16>(a, grid, s);
+  } else if (nv == 1) {
     AttnPartialKernel<G, 1><<<grid, kAttnWarps * 32, 0, s>>>(a);
   } else {
     AttnPartialKernel<G, 2><<<grid, kAttnWarps * 32, 0, s>>>(a);
