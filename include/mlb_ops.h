@@ -225,6 +225,18 @@ int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t k,
                         int64_t scratch_floats, void* stream);
 
 /*
+ * mlb_linear_rows_f32 for `count` (1..3) weight matrices applied to the same
+ * x in one launch — the q / k / v projections of a layer, or its FFN gate
+ * and up — sharing one split of x and one grid (small matrices no longer
+ * leave SMs idle): y[m] [t_rows, n[m]] = x . W[m]^T.  All matrices have
+ * format `qtype` and width k; scratch as for mlb_linear_rows_f32.
+ */
+int mlb_linear_rows_group_f32(int count, const void* const* w, int qtype,
+                              const int64_t* n, int64_t k, const float* x,
+                              int64_t t_rows, float* const* y, float* scratch,
+                              int64_t scratch_floats, void* stream);
+
+/*
  * Number of bounded device-side waits (a bulk weight copy that did not land
  * within the kernel's poll limit) that gave up on the current device since
  * the library was loaded.  A kernel that gives up leaves NaN in the outputs

@@ -34,7 +34,7 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxGroup = 8;      // query heads per kv head handled per CTA
 constexpr int kMaxHdVec = 2;      // float4 per lane: hd <= 256
-constexpr int kMinSlice = 64;     // positions per slice at least
+constexpr int kMinSlice = 128;    // positions per slice at least (4 warps x 32)
 
 struct AttnArgs {
   const float* q;

@@ -321,12 +321,27 @@ __device__ unsigned int g_tc_wait_timeouts;
 
 namespace {
 
+// Up to kMaxGroup weight matrices applied to the same x in one launch (the
+// q / k / v projections, the FFN gate / up): CTA i takes tile i of the
+// concatenated tile list, matrix by matrix, the token tile fastest so that
+// consecutive CTAs share a weight tile in L2.
+constexpr int kMaxGroup = 3;
+
+struct TcGroup {
+  CUtensorMap w[kMaxGroup];     // raw weight bytes of each matrix
+  CUtensorMap xh, xl;           // x's TF32 head and tail
+  float* y[kMaxGroup];
+  int n[kMaxGroup];
+  int tile_begin[kMaxGroup + 1];  // first tile of each matrix; [count] = total
+  int count;
+  int t_tiles;
+  int t_rows;
+  int k;
+};
+
 template <int QT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    LinearTcKernel(const __grid_constant__ CUtensorMap wmap,
-                   const __grid_constant__ CUtensorMap xhmap,
-                   const __grid_constant__ CUtensorMap xlmap, float* __restrict__ y, int n,
-                   int t_rows, int k) {
+    LinearTcKernel(const __grid_constant__ TcGroup grp) {
   constexpr int S = TcStages(QT);
   constexpr int kRaw = TcRawBytes(QT);
   constexpr int kBB = TcBlockBytes(QT);
@@ -351,9 +366,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTileRows;
-  const int t0 = blockIdx.y * kTileTokens;
-  const int steps = k / kStepK;
+  int mat = 0;
+  while (mat + 1 < grp.count && static_cast<int>(blockIdx.x) >= grp.tile_begin[mat + 1]) ++mat;
+  const int local = static_cast<int>(blockIdx.x) - grp.tile_begin[mat];
+  const int n0 = (local / grp.t_tiles) * kTileRows;
+  const int t0 = (local % grp.t_tiles) * kTileTokens;
+  const int n = grp.n[mat];
+  const int t_rows = grp.t_rows;
+  float* __restrict__ y = grp.y[mat];
+  const CUtensorMap* wmap = &grp.w[mat];
+  const int steps = grp.k / kStepK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -389,9 +411,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         MbarExpectTx(full(slot), kTileRows * kRaw + 2 * kTileBytes);
         const int xw = (s * kBB) & ~15;  // byte column of the block, rounded down
-        TmaLoad2D(SmemU32(raw + slot * kTileRows * kRaw), &wmap, xw, n0, full(slot));
-        TmaLoad2D(b_hi(slot), &xhmap, s * kStepK, t0, full(slot));
-        TmaLoad2D(b_lo(slot), &xlmap, s * kStepK, t0, full(slot));
+        TmaLoad2D(SmemU32(raw + slot * kTileRows * kRaw), wmap, xw, n0, full(slot));
+        TmaLoad2D(b_hi(slot), &grp.xh, s * kStepK, t0, full(slot));
+        TmaLoad2D(b_lo(slot), &grp.xl, s * kStepK, t0, full(slot));
         issued = s + 1;
       }
     }
@@ -544,17 +566,33 @@ bool Map2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_
 }
 
 template <int QT>
-int LaunchTc(const void* w, int64_t n, int64_t k, int64_t row_bytes, const float* xh,
-             const float* xl, int64_t t_rows, float* y, cudaStream_t s) {
-  CUtensorMap wmap, xhmap, xlmap;
-  if (!Map2D(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(row_bytes),
-             static_cast<uint64_t>(n), static_cast<uint64_t>(row_bytes), TcRawBytes(QT),
-             kTileRows,
-             QT == MLB_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !Map2D(&xhmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xh, static_cast<uint64_t>(k),
+int LaunchTc(int count, const void* const* w, const int64_t* n, int64_t k, int64_t row_bytes,
+             const float* xh, const float* xl, int64_t t_rows, float* const* y,
+             cudaStream_t s) {
+  TcGroup grp{};
+  grp.count = count;
+  grp.t_tiles = static_cast<int>((t_rows + kTileTokens - 1) / kTileTokens);
+  grp.t_rows = static_cast<int>(t_rows);
+  grp.k = static_cast<int>(k);
+  int64_t tiles = 0;
+  for (int m = 0; m < count; ++m) {
+    if (!Map2D(&grp.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, w[m],
+               static_cast<uint64_t>(row_bytes), static_cast<uint64_t>(n[m]),
+               static_cast<uint64_t>(row_bytes), TcRawBytes(QT), kTileRows,
+               QT == MLB_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: tensor map encoding failed");
+    grp.y[m] = y[m];
+    grp.n[m] = static_cast<int>(n[m]);
+    grp.tile_begin[m] = static_cast<int>(tiles);
+    tiles += (n[m] + kTileRows - 1) / kTileRows * grp.t_tiles;
+  }
+  grp.tile_begin[count] = static_cast<int>(tiles);
+  if (tiles > INT_MAX)
+    return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: too many tiles");
+  if (!Map2D(&grp.xh, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xh, static_cast<uint64_t>(k),
              static_cast<uint64_t>(t_rows), static_cast<uint64_t>(k) * 4, kStepK, kTileTokens,
              CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !Map2D(&xlmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xl, static_cast<uint64_t>(k),
+      !Map2D(&grp.xl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xl, static_cast<uint64_t>(k),
              static_cast<uint64_t>(t_rows), static_cast<uint64_t>(k) * 4, kStepK, kTileTokens,
              CU_TENSOR_MAP_SWIZZLE_128B))
     return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: tensor map encoding failed");
@@ -565,10 +603,7 @@ int LaunchTc(const void* w, int64_t n, int64_t k, int64_t row_bytes, const float
     cudaGetLastError();
     return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: shared memory opt-in");
   }
-  const dim3 grid(static_cast<unsigned>((n + kTileRows - 1) / kTileRows),
-                  static_cast<unsigned>((t_rows + kTileTokens - 1) / kTileTokens));
-  kernel<<<grid, kTcThreads, shm, s>>>(wmap, xhmap, xlmap, y, static_cast<int>(n),
-                                       static_cast<int>(t_rows), static_cast<int>(k));
+  kernel<<<static_cast<unsigned>(tiles), kTcThreads, shm, s>>>(grp);
   return CheckLaunch("mlb_linear_rows_f32");
 }
 
@@ -595,23 +630,53 @@ extern "C" int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows) {
   return 2 * k * t_rows + 8;  // xh, xl (+ room to align each to 16 bytes)
 }
 
-extern "C" int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t k,
-                                   const float* x, int64_t t_rows, float* y, float* scratch,
-                                   int64_t scratch_floats, void* stream) {
+namespace {
+
+// Shared by the single and grouped entries: W_m . x for m < count, all
+// matrices of the same format and width k.
+int LinearRowsGroup(int count, const void* const* w, int qtype, const int64_t* n, int64_t k,
+                    const float* x, int64_t t_rows, float* const* y, float* scratch,
+                    int64_t scratch_floats, void* stream) {
   using namespace mlb;
   if (qtype < MLB_F32 || qtype > MLB_Q4_1)
     return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: unknown qtype");
-  if (n < 0 || k <= 0 || k > INT_MAX || t_rows < 0 || n > INT_MAX || t_rows > INT_MAX)
+  if (count < 1 || count > kMaxGroup || w == nullptr || n == nullptr || y == nullptr)
+    return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: bad group");
+  if (k <= 0 || k > INT_MAX || t_rows < 0 || t_rows > INT_MAX)
     return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: bad shape");
-  if (n == 0 || t_rows == 0) return MLB_OK;
+  for (int m = 0; m < count; ++m)
+    if (n[m] < 0 || n[m] > INT_MAX) return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: bad shape");
+  if (t_rows == 0) return MLB_OK;
   const int64_t row_bytes = mlb_row_bytes(qtype, k);
-  const uintptr_t wp = reinterpret_cast<uintptr_t>(w);
-  const bool tc = t_rows >= kTcMinTokens && (k % kStepK) == 0 && (row_bytes % 16) == 0 &&
-                  (wp & 15u) == 0 && w != nullptr && x != nullptr && Aligned16(x);
-  if (!tc) return mlb_linear_f32(w, qtype, n, k, x, t_rows, y, stream);
-  if (y == nullptr) return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: null pointer");
+  bool tc = t_rows >= kTcMinTokens && (k % kStepK) == 0 && (row_bytes % 16) == 0 &&
+            x != nullptr && Aligned16(x);
+  for (int m = 0; m < count; ++m)
+    tc = tc && w[m] != nullptr && (reinterpret_cast<uintptr_t>(w[m]) & 15u) == 0;
+  if (!tc) {  // the GEMV form, matrix by matrix
+    for (int m = 0; m < count; ++m) {
+      if (n[m] == 0) continue;
+      const int rc = mlb_linear_f32(w[m], qtype, n[m], k, x, t_rows, y[m], stream);
+      if (rc != MLB_OK) return rc;
+    }
+    return MLB_OK;
+  }
+  for (int m = 0; m < count; ++m)
+    if (y[m] == nullptr && n[m] > 0) return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: null pointer");
   if (scratch == nullptr || scratch_floats < mlb_linear_rows_scratch_floats(k, t_rows))
     return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: scratch too small");
+  // matrices with rows (an empty one adds no tile)
+  const void* ws[kMaxGroup];
+  int64_t ns[kMaxGroup];
+  float* ys[kMaxGroup];
+  int used = 0;
+  for (int m = 0; m < count; ++m) {
+    if (n[m] == 0) continue;
+    ws[used] = w[m];
+    ns[used] = n[m];
+    ys[used] = y[m];
+    ++used;
+  }
+  if (used == 0) return MLB_OK;
   float* xh = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t{15});
   float* xl = xh + k * t_rows;  // k % 32 == 0: still 16-byte aligned
   cudaStream_t s = AsStream(stream);
@@ -619,13 +684,27 @@ extern "C" int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t 
   SplitTf32Kernel<<<static_cast<unsigned>((count4 + 255) / 256), 256, 0, s>>>(
       reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(xh),
       reinterpret_cast<uint4*>(xl), count4);
-  int rc = CheckLaunch("mlb_linear_rows_f32");
+  const int rc = CheckLaunch("mlb_linear_rows_f32");
   if (rc != MLB_OK) return rc;
   switch (qtype) {
-    case MLB_F32: return LaunchTc<MLB_F32>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
-    case MLB_Q8_0: return LaunchTc<MLB_Q8_0>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
-    case MLB_Q4_0: return LaunchTc<MLB_Q4_0>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
-    case MLB_Q4_1: return LaunchTc<MLB_Q4_1>(w, n, k, row_bytes, xh, xl, t_rows, y, s);
+    case MLB_F32: return LaunchTc<MLB_F32>(used, ws, ns, k, row_bytes, xh, xl, t_rows, ys, s);
+    case MLB_Q8_0: return LaunchTc<MLB_Q8_0>(used, ws, ns, k, row_bytes, xh, xl, t_rows, ys, s);
+    case MLB_Q4_0: return LaunchTc<MLB_Q4_0>(used, ws, ns, k, row_bytes, xh, xl, t_rows, ys, s);
+    default: return LaunchTc<MLB_Q4_1>(used, ws, ns, k, row_bytes, xh, xl, t_rows, ys, s);
   }
-  return Fail(MLB_ERR_ARG, "mlb_linear_rows_f32: unknown qtype");
+}
+
+}  // namespace
+
+extern "C" int mlb_linear_rows_f32(const void* w, int qtype, int64_t n, int64_t k,
+                                   const float* x, int64_t t_rows, float* y, float* scratch,
+                                   int64_t scratch_floats, void* stream) {
+  return LinearRowsGroup(1, &w, qtype, &n, k, x, t_rows, &y, scratch, scratch_floats, stream);
+}
+
+extern "C" int mlb_linear_rows_group_f32(int count, const void* const* w, int qtype,
+                                         const int64_t* n, int64_t k, const float* x,
+                                         int64_t t_rows, float* const* y, float* scratch,
+                                         int64_t scratch_floats, void* stream) {
+  return LinearRowsGroup(count, w, qtype, n, k, x, t_rows, y, scratch, scratch_floats, stream);
 }

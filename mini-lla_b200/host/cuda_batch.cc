@@ -6,7 +6,8 @@
 // one row, and every linear layer reads its whole weight matrix once per
 // token.  Here a pass takes up to max_rows tokens of consecutive positions
 // through the same steps as [rows, .] tensors: the linears read each weight
-// once per group of 8 rows (mlb_linear_f32), RMSNorm / SwiGLU / bias + RoPE /
+// on the tensor cores from 48 rows on (mlb_linear_rows_f32; q / k / v and
+// gate / up as one grouped launch each), RMSNorm / SwiGLU / bias + RoPE /
 // the K/V write / causal attention run once per layer over all rows, and
 // each residual add is fused into the RMSNorm that follows it.  Only the
 // last row of the batch goes through the final norm and the output
@@ -86,6 +87,11 @@ ModelRefs Resolve(const Model& model) {
   return refs;
 }
 
+// Weights that can share one grouped linear launch (same format and width).
+bool SameShape(const CudaWeight& a, const CudaWeight& b) {
+  return a.type == b.type && a.cols == b.cols;
+}
+
 void Check(int rc, const char* caller) {
   if (rc == MLB_OK) return;
   const std::string message = std::string(caller) + ": " + mlb_last_error();
@@ -155,9 +161,17 @@ Tensor ForwardBatchCuda(Context& context, const Model& model, const MiniBatch& b
         norm = CudaAddRmsNormRows(ffn, &x, *l.attention_norm, eps, &h);
         x = std::move(h);
       }
-      CudaTensor q = CudaLinearRows(norm, *l.wq);
-      CudaTensor k = CudaLinearRows(norm, *l.wk);
-      CudaTensor v = CudaLinearRows(norm, *l.wv);
+      CudaTensor q, k, v;
+      if (SameShape(*l.wq, *l.wk) && SameShape(*l.wq, *l.wv)) {  // one launch
+        std::vector<CudaTensor> qkv = CudaLinearRowsGroup(norm, {l.wq, l.wk, l.wv});
+        q = std::move(qkv[0]);
+        k = std::move(qkv[1]);
+        v = std::move(qkv[2]);
+      } else {
+        q = CudaLinearRows(norm, *l.wq);
+        k = CudaLinearRows(norm, *l.wk);
+        v = CudaLinearRows(norm, *l.wv);
+      }
       if (l.bv != nullptr) v = CudaAddBiasRows(v, l.bv);
       CudaRopeRows(&q, &k, l.bq, l.bk, positions, config.rope_theta, config.n_heads,
                    config.n_kv_heads, head_dim, config.rope_type);
@@ -169,8 +183,13 @@ Tensor ForwardBatchCuda(Context& context, const Model& model, const MiniBatch& b
       CudaTensor x_attn;  // x + attention output
       const CudaTensor ffn_norm =
           CudaAddRmsNormRows(projected, &x, *l.ffn_norm, eps, &x_attn);
-      const CudaTensor act = CudaSwiGlu(CudaLinearRows(ffn_norm, *l.w_gate),
-                                        CudaLinearRows(ffn_norm, *l.w_up));
+      CudaTensor act;
+      if (SameShape(*l.w_gate, *l.w_up)) {
+        const std::vector<CudaTensor> gate_up = CudaLinearRowsGroup(ffn_norm, {l.w_gate, l.w_up});
+        act = CudaSwiGlu(gate_up[0], gate_up[1]);
+      } else {
+        act = CudaSwiGlu(CudaLinearRows(ffn_norm, *l.w_gate), CudaLinearRows(ffn_norm, *l.w_up));
+      }
       ffn = CudaLinearRows(act, *l.w_down);
       x = std::move(x_attn);
     }

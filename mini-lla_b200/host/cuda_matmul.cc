@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "mini_llama/cuda_layer_ops.h"
 #include "mlb_ops.h"
@@ -72,6 +73,46 @@ CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight) {
     throw std::runtime_error(message);
   }
   return output;
+}
+
+std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
+                                            const std::vector<const CudaWeight*>& weights) {
+  if (weights.empty() || weights.size() > 3) {
+    throw std::invalid_argument("CudaLinearRowsGroup: 1 to 3 weights");
+  }
+  const CudaWeight& first = *weights.front();
+  for (const CudaWeight* w : weights) {
+    if (w == nullptr || w->type != first.type || w->cols != first.cols) {
+      throw std::invalid_argument("CudaLinearRowsGroup: weights differ in format or width");
+    }
+  }
+  if (first.cols <= 0 || x.shape().empty() || x.shape().back() != first.cols) {
+    throw std::invalid_argument("CudaLinearRowsGroup: input size mismatch");
+  }
+  const int rows = static_cast<int>(x.Size() / static_cast<size_t>(first.cols));
+  std::vector<CudaTensor> outputs;
+  const void* w[3];
+  int64_t n[3];
+  float* y[3];
+  for (size_t m = 0; m < weights.size(); ++m) {
+    outputs.emplace_back(std::vector<int>{rows, weights[m]->rows});
+    w[m] = weights[m]->buffer.data();
+    n[m] = weights[m]->rows;
+    y[m] = outputs.back().data();
+  }
+  if (rows == 0) return outputs;
+  const int64_t need = mlb_linear_rows_scratch_floats(first.cols, rows);
+  DeviceBuffer scratch;
+  scratch.Reset(static_cast<size_t>(need) * sizeof(float));
+  const int rc = mlb_linear_rows_group_f32(
+      static_cast<int>(weights.size()), w, QType(first.type), n, first.cols, x.data(), rows, y,
+      static_cast<float*>(scratch.data()), need, nullptr);
+  if (rc != MLB_OK) {
+    const std::string message = std::string("CudaLinearRowsGroup: ") + mlb_last_error();
+    if (rc == MLB_ERR_ARG) throw std::invalid_argument(message);
+    throw std::runtime_error(message);
+  }
+  return outputs;
 }
 
 }  // namespace mini_lla

@@ -57,6 +57,13 @@ CudaTensor CudaEmbeddingRows(const CudaWeight& embedding,
 // weight.rows] (CudaLinear, cuda_matmul.h, for a batch of tokens).
 CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight);
 
+// CudaLinearRows for up to three weights applied to the same x (the q / k /
+// v projections, the FFN gate / up) in one launch: one TF32 split of x and
+// one grid for all of them.  The weights must share format and width
+// (std::invalid_argument otherwise).
+std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
+                                            const std::vector<const CudaWeight*>& weights);
+
 // value[r] + bias for every row of value [rows, bias size] (AddBias,
 // forward.cc:36-47, for a batch of tokens); a null bias copies value.
 CudaTensor CudaAddBiasRows(const CudaTensor& value, const CudaWeight* bias);

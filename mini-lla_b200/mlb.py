@@ -54,6 +54,9 @@ SIGNATURES = {
     "mlb_linear_rows_scratch_floats": (c_int64, [c_int64, c_int64]),
     "mlb_linear_rows_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                     c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
+    "mlb_linear_rows_group_f32": (c_int, [c_int, c_void_p, c_int, c_void_p, c_int64,
+                                          c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+                                          c_void_p]),
     "mlb_attention_rows_scratch_floats": (c_int64, [c_int, c_int, c_int, c_int64,
                                                     c_int64]),
     "mlb_attention_rows_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p,
@@ -426,6 +429,33 @@ def linear_rows(weight, qtype: int, n: int, k: int, x, out=None, scratch=None,
                                       _ptr(out), _ptr(scratch), scratch.numel(),
                                       _stream(stream)), op)
     return out
+
+
+def linear_rows_group(weights, qtype: int, ns, k: int, x, scratch=None, stream=None):
+    """[x . dequant(W_m)^T for each W_m] in one launch (up to 3 matrices of
+    the same format and width k)."""
+    import torch
+    op = "linear_rows_group"
+    _f32_cuda(x, op, "x")
+    _require(x.shape[-1] == k, op, "input size mismatch")
+    _require(1 <= len(weights) == len(ns) <= 3, op, "1 to 3 matrices")
+    t_rows = x.numel() // k
+    outs = [torch.empty((t_rows, n), dtype=torch.float32, device=x.device) for n in ns]
+    for w, n in zip(weights, ns):
+        _require(w.is_cuda and w.is_contiguous(), op, "weights must be contiguous CUDA tensors")
+        _require(w.numel() * w.element_size() >= n * row_bytes(qtype, k), op,
+                 "weight smaller than n rows")
+    need = load().mlb_linear_rows_scratch_floats(k, t_rows)
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.float32, device=x.device)
+    count = len(weights)
+    wp = (ctypes.c_void_p * count)(*[w.data_ptr() for w in weights])
+    na = (ctypes.c_int64 * count)(*ns)
+    yp = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
+    _check(load().mlb_linear_rows_group_f32(count, wp, qtype, na, k, _ptr(x), t_rows, yp,
+                                            _ptr(scratch), scratch.numel(), _stream(stream)),
+           op)
+    return outs
 
 
 def status_check(status, stream=None) -> int:

@@ -120,3 +120,24 @@ def test_linear_rows_large_values_and_small_batches(cuda, oracle):
         got = mlb.linear_rows(dev(table, cuda), wl.Q8_0, n, k, dev(x, cuda))
         torch.cuda.synchronize()
         _check(got.cpu().numpy(), want, wdeq, x, f"rows wide-range t={t}")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_1, wl.F32])
+@pytest.mark.parametrize("t", [5, 64, 200])
+def test_linear_rows_group_vs_single(cuda, oracle, qtype, t):
+    """Three matrices of different heights (a q / k / v shape) in one grouped
+    launch: each output within the same bar as the single-matrix entry; below
+    48 tokens the group falls back to the GEMV per matrix."""
+    import torch
+    rng = np.random.default_rng(t + qtype)
+    k = 512
+    ns = (256, 128, 130)
+    tables = [wl.numpy_quant_table(qtype, n, k, seed=n + t) for n in ns]
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    outs = mlb.linear_rows_group([dev(tb, cuda) for tb in tables], qtype, list(ns), k,
+                                 dev(x, cuda))
+    torch.cuda.synchronize()
+    for tb, n, got in zip(tables, ns, outs):
+        want = oracle.linear(tb, qtype, n, k, x)
+        wdeq, _ = oracle.embedding(tb, qtype, n, k, np.arange(n, dtype=np.int32))
+        _check(got.cpu().numpy(), want, wdeq, x, f"group {wl.QNAME[qtype]} n={n} t={t}")
