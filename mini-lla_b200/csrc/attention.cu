@@ -427,19 +427,25 @@ int ValidateAttention(const float* q, const float* keys, const float* values,
 // ---------------------------------------------------------------------------
 // Prompt chunks: tiles of query rows.
 //
-// CTA (kv head g, tile of QR = 64 / G consecutive query rows) holds the
-// QV = QR * G query vectors of its rows and group in shared memory and walks
-// the visible positions in blocks of 32 keys: every K/V block is staged once
+// CTA (kv head g, tile of QR = 64 / G consecutive query rows; tiles of the
+// most keys first) holds the QV = QR * G <= 64 query vectors of its rows and
+// group in shared memory and walks
+// the visible positions in blocks of 64 keys: every K/V block is staged once
 // (cp.async, double-buffered) for all QV query vectors instead of once per
-// query row.  256 threads; thread (pair p = tid / 8, j = tid % 8) scores
-// query vectors 2p, 2p + 1 against keys j, j + 8, j + 16, j + 24 of a block
-// (rows padded by 16 bytes so those reads hit distinct banks), keeps the
-// online softmax of its two vectors (max / sum reduced over the 8 threads of
-// the pair) and accumulates P.V for float4 columns j, j + 8, ... of them.
-// Masked (future) keys score -inf; no slice partials, no combine kernel.
-constexpr int kTileKeys = 32;
+// query row.  256 threads, each owning 4 query vectors x 4 keys of the score
+// tile (thread (a = tid / 16, b = tid % 16): vectors 4a .. 4a + 3, keys
+// b, b + 16, b + 32, b + 48): 8 shared loads feed 64 FMAs per 4 dimensions.
+// Rows are padded by 16 bytes so the 8 keys of a quarter-warp sit on
+// distinct banks.  The online softmax of a vector is reduced over the 16
+// threads that share it; the probabilities go to shared memory transposed
+// ([key][vector]) so that P.V reads the 4 probabilities of a thread's
+// vectors with one 16-byte load, and each thread accumulates its 4 vectors
+// x float4 columns c, c + 16, ... of the output.  Future keys score -inf;
+// no slice partials.
+constexpr int kTileKeys = 64;
 constexpr int kTileQv = 64;
 constexpr int kTileThreads = 256;
+constexpr int kPsStride = kTileQv + 4;  // transposed probability tile row
 
 struct AttnTileArgs {
   const float* q;
@@ -460,38 +466,37 @@ __host__ __device__ constexpr int TileRowFloats() { return 4 * HD4 + 4; }  // on
 template <int G, int HD4>
 constexpr size_t TileSmemBytes() {
   return sizeof(float) * (static_cast<size_t>(kTileQv + 4 * kTileKeys) * TileRowFloats<HD4>() +
-                          static_cast<size_t>(kTileQv) * (kTileKeys + 1));
+                          static_cast<size_t>(kTileKeys) * kPsStride);
 }
 
 template <int G, int HD4>
-__global__ void __launch_bounds__(kTileThreads) AttnRowTileKernel(AttnTileArgs a) {
+__global__ void __launch_bounds__(kTileThreads, 1) AttnRowTileKernel(AttnTileArgs a) {
   constexpr int QR = kTileQv / G;  // query rows per CTA
   constexpr int QV = QR * G;
   constexpr int RF = TileRowFloats<HD4>();
   constexpr int HD = 4 * HD4;
-  constexpr int CPT = HD4 / 8;     // float4 columns per thread in P.V
+  constexpr int CPT = HD4 / 16;    // float4 columns per thread in P.V (1 or 2)
   extern __shared__ __align__(16) float tsm[];
   float* qs = tsm;                           // [QV][RF]
   float* ks = qs + kTileQv * RF;             // [2][kTileKeys][RF]
   float* vs = ks + 2 * kTileKeys * RF;       // [2][kTileKeys][RF]
-  float* ps = vs + 2 * kTileKeys * RF;       // [QV][kTileKeys + 1]
+  float* ps = vs + 2 * kTileKeys * RF;       // [kTileKeys][kPsStride]
 
   const int g = blockIdx.x;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * QR;
+  // the last row tiles see the most keys: schedule them first
+  const int64_t r0 = static_cast<int64_t>(gridDim.y - 1 - blockIdx.y) * QR;
   const int tid = threadIdx.x;
-  const int pair = tid >> 3;
-  const int j = tid & 7;
-  const int v0 = 2 * pair, v1 = 2 * pair + 1;
-  const bool active = v1 < QV;  // (QV is even: both or neither)
+  const int qa = tid >> 4;   // vectors 4 qa .. 4 qa + 3
+  const int kb4 = tid & 15;  // keys kb4 + 16 j (scores); float4 columns kb4 + 16 c (P.V)
   const int64_t row_stride = static_cast<int64_t>(a.n_heads) * HD;
   const int64_t kv_stride = static_cast<int64_t>(a.n_kv_heads) * HD;
 
   // the tile's query vectors (rows beyond the chunk read as zeros)
-  for (int i = tid; i < QV * HD4; i += kTileThreads) {
+  for (int i = tid; i < kTileQv * HD4; i += kTileThreads) {
     const int v = i / HD4, d4 = i - v * HD4;
     const int64_t row = r0 + v / G;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < a.rows)
+    if (v < QV && row < a.rows)
       x = *reinterpret_cast<const float4*>(a.q + row * row_stride +
                                            static_cast<int64_t>(g * G + v % G) * HD + 4 * d4);
     *reinterpret_cast<float4*>(qs + v * RF + 4 * d4) = x;
@@ -514,14 +519,17 @@ __global__ void __launch_bounds__(kTileThreads) AttnRowTileKernel(AttnTileArgs a
     }
   };
 
-  const int64_t qpos0 = a.position + r0 + v0 / G;  // positions of the two vectors
-  const int64_t qpos1 = a.position + r0 + v1 / G;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  float4 acc0[CPT], acc1[CPT];
+  int64_t qpos[4];
+  float m[4], l[4];
+  float4 acc[4][CPT];
 #pragma unroll
-  for (int c = 0; c < CPT; ++c) {
-    acc0[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    acc1[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * qa + i;
+    qpos[i] = v < QV ? a.position + r0 + v / G : -1;  // padding vectors see nothing
+    m[i] = -INFINITY;
+    l[i] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[i][c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 
   stage(0);
@@ -533,106 +541,108 @@ __global__ void __launch_bounds__(kTileThreads) AttnRowTileKernel(AttnTileArgs a
     __syncthreads();  // block b (and, on b == 0, the query tile) in place
     const float* kb = ks + (b & 1) * kTileKeys * RF;
     const float* vb = vs + (b & 1) * kTileKeys * RF;
-    if (active) {
-      float s0[4], s1[4];
+    float sc[4][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) s0[i] = s1[i] = 0.0f;
-#pragma unroll 4
-      for (int d4 = 0; d4 < HD4; ++d4) {
-        const float4 qa = *reinterpret_cast<const float4*>(qs + v0 * RF + 4 * d4);
-        const float4 qb = *reinterpret_cast<const float4*>(qs + v1 * RF + 4 * d4);
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 kk = *reinterpret_cast<const float4*>(kb + (j + 8 * i) * RF + 4 * d4);
-          s0[i] = fmaf(qa.x, kk.x, s0[i]);
-          s0[i] = fmaf(qa.y, kk.y, s0[i]);
-          s0[i] = fmaf(qa.z, kk.z, s0[i]);
-          s0[i] = fmaf(qa.w, kk.w, s0[i]);
-          s1[i] = fmaf(qb.x, kk.x, s1[i]);
-          s1[i] = fmaf(qb.y, kk.y, s1[i]);
-          s1[i] = fmaf(qb.z, kk.z, s1[i]);
-          s1[i] = fmaf(qb.w, kk.w, s1[i]);
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int d4 = 0; d4 < HD4; ++d4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        qv[i] = *reinterpret_cast<const float4*>(qs + (4 * qa + i) * RF + 4 * d4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        kv[j] = *reinterpret_cast<const float4*>(kb + (kb4 + 16 * j) * RF + 4 * d4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
         }
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+    }
+    // online softmax of each of the 4 vectors over the block's 64 keys
+    // (16 threads share a vector: lanes 0-15 or 16-31 of a warp)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t t = static_cast<int64_t>(b) * kTileKeys + j + 8 * i;
-        s0[i] = t <= qpos0 ? __fmul_rn(s0[i], a.scale) : -INFINITY;
-        s1[i] = t <= qpos1 ? __fmul_rn(s1[i], a.scale) : -INFINITY;
-        mx0 = fmaxf(mx0, s0[i]);
-        mx1 = fmaxf(mx1, s1[i]);
+    for (int i = 0; i < 4; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t t = static_cast<int64_t>(b) * kTileKeys + kb4 + 16 * j;
+        sc[i][j] = t <= qpos[i] ? __fmul_rn(sc[i][j], a.scale) : -INFINITY;
+        mx = fmaxf(mx, sc[i][j]);
       }
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
-      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float nm = fmaxf(m[i], mx);
       // a vector with no visible key yet keeps p = 0 (no -inf - -inf)
-      const float al0 = n0 == -INFINITY ? 1.0f : expf(m0 - n0);
-      const float al1 = n1 == -INFINITY ? 1.0f : expf(m1 - n1);
-      float sum0 = 0.0f, sum1 = 0.0f;
+      const float al = nm == -INFINITY ? 1.0f : expf(m[i] - nm);
+      float sum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float p0 = s0[i] == -INFINITY ? 0.0f : expf(s0[i] - n0);
-        const float p1 = s1[i] == -INFINITY ? 0.0f : expf(s1[i] - n1);
-        ps[v0 * (kTileKeys + 1) + j + 8 * i] = p0;
-        ps[v1 * (kTileKeys + 1) + j + 8 * i] = p1;
-        sum0 += p0;
-        sum1 += p1;
+      for (int j = 0; j < 4; ++j) {
+        sc[i][j] = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - nm);  // now p
+        sum += sc[i][j];
       }
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        sum0 += __shfl_xor_sync(0xffffffffu, sum0, o);
-        sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
-      }
-      l0 = fmaf(l0, al0, sum0);
-      l1 = fmaf(l1, al1, sum1);
-      m0 = n0;
-      m1 = n1;
+      for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l[i] = fmaf(l[i], al, sum);
+      m[i] = nm;
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
-        acc0[c].x *= al0; acc0[c].y *= al0; acc0[c].z *= al0; acc0[c].w *= al0;
-        acc1[c].x *= al1; acc1[c].y *= al1; acc1[c].z *= al1; acc1[c].w *= al1;
-      }
-      __syncwarp();  // the pair's p values are in place (the 8 threads share a warp)
-#pragma unroll 4
-      for (int key = 0; key < kTileKeys; ++key) {
-        const float p0 = ps[v0 * (kTileKeys + 1) + key];
-        const float p1 = ps[v1 * (kTileKeys + 1) + key];
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-          const float4 vv = *reinterpret_cast<const float4*>(vb + key * RF + 4 * (j + 8 * c));
-          acc0[c].x = fmaf(p0, vv.x, acc0[c].x);
-          acc0[c].y = fmaf(p0, vv.y, acc0[c].y);
-          acc0[c].z = fmaf(p0, vv.z, acc0[c].z);
-          acc0[c].w = fmaf(p0, vv.w, acc0[c].w);
-          acc1[c].x = fmaf(p1, vv.x, acc1[c].x);
-          acc1[c].y = fmaf(p1, vv.y, acc1[c].y);
-          acc1[c].z = fmaf(p1, vv.z, acc1[c].z);
-          acc1[c].w = fmaf(p1, vv.w, acc1[c].w);
-        }
+        acc[i][c].x *= al;
+        acc[i][c].y *= al;
+        acc[i][c].z *= al;
+        acc[i][c].w *= al;
       }
     }
-    __syncthreads();  // buffers of block b are free for block b + 2
+    // probabilities, transposed: ps[key][vector]
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(ps + (kb4 + 16 * j) * kPsStride + 4 * qa) =
+          make_float4(sc[0][j], sc[1][j], sc[2][j], sc[3][j]);
+    __syncthreads();  // every vector's probabilities are in place
+#pragma unroll 4
+    for (int key = 0; key < kTileKeys; ++key) {
+      const float4 p = *reinterpret_cast<const float4*>(ps + key * kPsStride + 4 * qa);
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        const float4 vv = *reinterpret_cast<const float4*>(vb + key * RF + 4 * (kb4 + 16 * c));
+        acc[0][c].x = fmaf(p.x, vv.x, acc[0][c].x);
+        acc[0][c].y = fmaf(p.x, vv.y, acc[0][c].y);
+        acc[0][c].z = fmaf(p.x, vv.z, acc[0][c].z);
+        acc[0][c].w = fmaf(p.x, vv.w, acc[0][c].w);
+        acc[1][c].x = fmaf(p.y, vv.x, acc[1][c].x);
+        acc[1][c].y = fmaf(p.y, vv.y, acc[1][c].y);
+        acc[1][c].z = fmaf(p.y, vv.z, acc[1][c].z);
+        acc[1][c].w = fmaf(p.y, vv.w, acc[1][c].w);
+        acc[2][c].x = fmaf(p.z, vv.x, acc[2][c].x);
+        acc[2][c].y = fmaf(p.z, vv.y, acc[2][c].y);
+        acc[2][c].z = fmaf(p.z, vv.z, acc[2][c].z);
+        acc[2][c].w = fmaf(p.z, vv.w, acc[2][c].w);
+        acc[3][c].x = fmaf(p.w, vv.x, acc[3][c].x);
+        acc[3][c].y = fmaf(p.w, vv.y, acc[3][c].y);
+        acc[3][c].z = fmaf(p.w, vv.z, acc[3][c].z);
+        acc[3][c].w = fmaf(p.w, vv.w, acc[3][c].w);
+      }
+    }
+    __syncthreads();  // buffers of block b and the probability tile are free
   }
   CopyAsyncWait<0>();
-  if (!active) return;
-  const int64_t row0 = r0 + v0 / G, row1 = r0 + v1 / G;
-  float* o0 = a.out + row0 * row_stride + static_cast<int64_t>(g * G + v0 % G) * HD;
-  float* o1 = a.out + row1 * row_stride + static_cast<int64_t>(g * G + v1 % G) * HD;
 #pragma unroll
-  for (int c = 0; c < CPT; ++c) {
-    const int col = 4 * (j + 8 * c);
-    if (row0 < a.rows)
-      *reinterpret_cast<float4*>(o0 + col) =
-          make_float4(__fdiv_rn(acc0[c].x, l0), __fdiv_rn(acc0[c].y, l0),
-                      __fdiv_rn(acc0[c].z, l0), __fdiv_rn(acc0[c].w, l0));
-    if (row1 < a.rows)
-      *reinterpret_cast<float4*>(o1 + col) =
-          make_float4(__fdiv_rn(acc1[c].x, l1), __fdiv_rn(acc1[c].y, l1),
-                      __fdiv_rn(acc1[c].z, l1), __fdiv_rn(acc1[c].w, l1));
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * qa + i;
+    const int64_t row = r0 + v / G;
+    if (v >= QV || row >= a.rows) continue;
+    float* o = a.out + row * row_stride + static_cast<int64_t>(g * G + v % G) * HD;
+#pragma unroll
+    for (int c = 0; c < CPT; ++c)
+      *reinterpret_cast<float4*>(o + 4 * (kb4 + 16 * c)) =
+          make_float4(__fdiv_rn(acc[i][c].x, l[i]), __fdiv_rn(acc[i][c].y, l[i]),
+                      __fdiv_rn(acc[i][c].z, l[i]), __fdiv_rn(acc[i][c].w, l[i]));
   }
 }
 
@@ -654,33 +664,34 @@ int LaunchRowTile(const AttnTileArgs& a, cudaStream_t s) {
 }
 
 // Row tiles when they fill the GPU (n_kv_heads x row tiles >= half the SMs),
-// group 1 / 2 / 4 / 8, head_dim 64 or 128; -1 when the shape does not fit.
+// group 1 .. 8, head_dim 64 or 128; -1 when the shape does not fit.
+template <int HD4>
+int LaunchRowTiles(const AttnTileArgs& a, int group, cudaStream_t s) {
+  switch (group) {
+    case 1: return LaunchRowTile<1, HD4>(a, s);
+    case 2: return LaunchRowTile<2, HD4>(a, s);
+    case 3: return LaunchRowTile<3, HD4>(a, s);
+    case 4: return LaunchRowTile<4, HD4>(a, s);
+    case 5: return LaunchRowTile<5, HD4>(a, s);
+    case 6: return LaunchRowTile<6, HD4>(a, s);
+    case 7: return LaunchRowTile<7, HD4>(a, s);
+    default: return LaunchRowTile<8, HD4>(a, s);
+  }
+}
+
 int AttentionRowTiles(const float* q, const float* keys, const float* values, float* out,
                       int64_t position, int64_t rows, int64_t max_seq, int n_heads,
                       int n_kv_heads, int hd, cudaStream_t s) {
   const int group = n_heads / n_kv_heads;
-  if ((group != 1 && group != 2 && group != 4 && group != 8) || (hd != 64 && hd != 128) ||
-      !Aligned16(out) || rows > 65535LL * (kTileQv / group))
+  if (group < 1 || group > 8 || (hd != 64 && hd != 128) || !Aligned16(out) ||
+      rows > 65535LL * (kTileQv / group))
     return -1;
   if (static_cast<int64_t>(n_kv_heads) * ((rows + kTileQv / group - 1) / (kTileQv / group)) <
       SmCount() / 2)
     return -1;
   AttnTileArgs a{q, keys, values, out, position, rows, max_seq, n_heads, n_kv_heads,
                  1.0f / std::sqrt(static_cast<float>(hd))};
-  if (hd == 64) {
-    switch (group) {
-      case 1: return LaunchRowTile<1, 16>(a, s);
-      case 2: return LaunchRowTile<2, 16>(a, s);
-      case 4: return LaunchRowTile<4, 16>(a, s);
-      default: return LaunchRowTile<8, 16>(a, s);
-    }
-  }
-  switch (group) {
-    case 1: return LaunchRowTile<1, 32>(a, s);
-    case 2: return LaunchRowTile<2, 32>(a, s);
-    case 4: return LaunchRowTile<4, 32>(a, s);
-    default: return LaunchRowTile<8, 32>(a, s);
-  }
+  return hd == 64 ? LaunchRowTiles<16>(a, group, s) : LaunchRowTiles<32>(a, group, s);
 }
 
 // Shared by the entry points: scratch must hold AttentionScratchFloats() for

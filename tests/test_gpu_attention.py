@@ -143,7 +143,9 @@ def torch_zeros(shape, device):
     (32, 32, 128, 100, 300, 512),   # group 1, partial last tile
     (16, 2, 64, 7, 1000, 1100),     # group 8, head_dim 64
     (64, 32, 128, 1500, 100, 1700), # group 2, chunk after a long context
-    (32, 8, 64, 33, 333, 400)])     # head_dim 64, ragged everything
+    (32, 8, 64, 33, 333, 400),      # head_dim 64, ragged everything
+    (28, 4, 128, 0, 700, 800),      # group 7 (Qwen2-7B): 9 rows = 63 vectors per tile
+    (24, 8, 64, 10, 400, 500)])     # group 3: 21 rows = 63 vectors
 def test_attention_row_tiles_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max_seq):
     """Prompt chunks large enough for the query-row tile kernel (n_kv_heads x
     row tiles >= half the SMs): sampled rows (first, last, tile edges, random)
