@@ -366,8 +366,52 @@ __device__ __forceinline__ void BulkGroup(const uint8_t* blk, const float4* x, i
   }
 }
 
+// One group of 8 blocks for the ggml formats: lane l takes block l / 4 and
+// its float4 chunks j = l % 4 and j + 4 (values 4j .. 4j + 3 and
+// 16 + 4j .. 16 + 4j + 3; for Q4 both come from the same 4 code bytes).  x
+// of an odd block is staged with its chunk halves swapped, so xa / xb (this
+// lane's two x chunks of token 0) are conflict-free across a quarter-warp.
 template <int QT, int T>
-__global__ void __launch_bounds__(kBulkMaxWarps * 32)
+__device__ __forceinline__ void BulkGroup8(const uint8_t* blk, const float4* xa,
+                                           const float4* xb, int k4, int j,
+                                           uint64_t (&acc)[T]) {
+  uint32_t lo, hi;  // code words of chunks j and j + 4
+  float bias;
+  if (QT == MLB_Q8_0) {
+    lo = (Smem16(blk + 2 + 4 * j) | (Smem16(blk + 4 + 4 * j) << 16)) ^ 0x80808080u;
+    hi = (Smem16(blk + 18 + 4 * j) | (Smem16(blk + 20 + 4 * j) << 16)) ^ 0x80808080u;
+    bias = 8388736.0f;
+  } else {
+    const uint32_t u = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * j)
+                                      : (Smem16(blk + 2 + 4 * j) | (Smem16(blk + 4 + 4 * j) << 16));
+    lo = u & 0x0F0F0F0Fu;
+    hi = (u >> 4) & 0x0F0F0F0Fu;
+    bias = QT == MLB_Q4_0 ? 8388616.0f : 8388608.0f;
+  }
+  uint64_t a01, a23, b01, b23;
+  BytesToPairs(lo, bias, a01, a23);
+  BytesToPairs(hi, bias, b01, b23);
+  const uint32_t scale = QT == MLB_Q4_1 ? *reinterpret_cast<const uint32_t*>(blk) : Smem16(blk);
+  const float d = HalfBits(scale & 0xffffu);
+  const uint64_t d2 = Pack2(d, d);
+  const float m = QT == MLB_Q4_1 ? HalfBits(scale >> 16) : 0.0f;
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    const float4 va = xa[t * k4], vb = xb[t * k4];
+    const uint64_t xa01 = Pack2(va.x, va.y), xa23 = Pack2(va.z, va.w);
+    const uint64_t xb01 = Pack2(vb.x, vb.y), xb23 = Pack2(vb.z, vb.w);
+    uint64_t p = Mul2(a01, xa01);
+    p = Fma2(a23, xa23, p);
+    p = Fma2(b01, xb01, p);
+    p = Fma2(b23, xb23, p);
+    acc[t] = Fma2(d2, p, acc[t]);
+    if (QT == MLB_Q4_1)
+      acc[t] = Fma2(Pack2(m, m), Add2(Add2(xa01, xa23), Add2(xb01, xb23)), acc[t]);
+  }
+}
+
+template <int QT, int T>
+__global__ void __launch_bounds__(kBulkMaxWarps * 32, 1)
     GemvBulkKernel(GemvArgs a, int sb, int slot_bytes) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int kBB = BlockBytes<QT>();
@@ -381,10 +425,12 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32)
   uint8_t* ring = smem + kBarBytes + static_cast<size_t>(T) * a.k * 4 +
                   static_cast<size_t>(warp) * kBulkStages * slot_bytes;
 
-  {  // x for every token, once per CTA
+  {  // x for every token, once per CTA (ggml formats: odd blocks' chunk
+     // halves swapped, see BulkGroup8)
     float4* xd = reinterpret_cast<float4*>(smem + kBarBytes);
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    for (int i = threadIdx.x; i < T * k4; i += blockDim.x) CopyAsync16(xd + i, x4 + i);
+    for (int i = threadIdx.x; i < T * k4; i += blockDim.x)
+      CopyAsync16(xd + (QT == MLB_F32 ? i : (i ^ ((i & 8) >> 1))), x4 + i);
     CopyAsyncCommit();
   }
   if (lane == 0) {
@@ -448,15 +494,39 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32)
     while (b < count) {
       // blocks left in this segment and in the current row (multiples of 4)
       const int run = count - b < nb - kb ? count - b : nb - kb;
-      const uint8_t* blk = slot + (b + (lane >> 3)) * kBB;
-      const float4* xg = xs + kb * 8 + lane;  // this lane's x float4
       int i = 0;
-      // two independent groups of 4 blocks per step (ILP across the chains)
-      for (; i + 8 <= run; i += 8) {
-        BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
-        BulkGroup<QT, T>(blk + (i + 4) * kBB, xg + (i + 4) * 8, k4, lane, acc2);
+      if (QT == MLB_F32) {
+        const uint8_t* blk = slot + (b + (lane >> 3)) * kBB;
+        const float4* xg = xs + kb * 8 + lane;  // this lane's x float4
+        // two independent groups of 4 blocks per step (ILP across the chains)
+        for (; i + 8 <= run; i += 8) {
+          BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
+          BulkGroup<QT, T>(blk + (i + 4) * kBB, xg + (i + 4) * 8, k4, lane, acc2);
+        }
+        if (i < run) BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
+      } else {
+        // groups of 8 blocks, 4 lanes per block (kb is even here: block
+        // parity = (lane / 4) & 1)
+        const int j = lane & 3;
+        const int par = (lane >> 2) & 1;
+        const uint8_t* blk8 = slot + (b + (lane >> 2)) * kBB;
+        const float4* xa = xs + (kb + (lane >> 2)) * 8 + j + 4 * par;
+        const float4* xb = xs + (kb + (lane >> 2)) * 8 + j + 4 * (1 - par);
+        for (; i + 16 <= run; i += 16) {
+          BulkGroup8<QT, T>(blk8 + i * kBB, xa + i * 8, xb + i * 8, k4, j, acc);
+          BulkGroup8<QT, T>(blk8 + (i + 8) * kBB, xa + (i + 8) * 8, xb + (i + 8) * 8, k4, j,
+                            acc2);
+        }
+        if (i + 8 <= run) {
+          BulkGroup8<QT, T>(blk8 + i * kBB, xa + i * 8, xb + i * 8, k4, j, acc);
+          i += 8;
+        }
+        if (i < run) {  // 4 blocks left: 8 lanes per block
+          const float4* xg = xs + (kb + i + (lane >> 3)) * 8 +
+                             ((lane & 7) ^ (((lane >> 3) & 1) << 2));
+          BulkGroup<QT, T>(slot + (b + i + (lane >> 3)) * kBB, xg, k4, lane, acc);
+        }
       }
-      if (i < run) BulkGroup<QT, T>(blk + i * kBB, xg + i * 8, k4, lane, acc);
       b += run;
       kb += run;
       if (kb == nb) {
