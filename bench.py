@@ -247,9 +247,17 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
             return None  # head-major rows: copied whole with the last chunk
         return slice(r0, r1)
 
+    # a chunk's inputs of the next step overwrite its buffers (q / k in
+    # place) only once the previous step has read that chunk back: per-chunk
+    # events, so the next step's uploads overlap this step's readback
+    prev_out = [None] * chunks
+    whole = any(rows_of(k, 0, 1) is None for k in in_keys + out_keys)
+
     def one_step():
         done_in = []
         for c, (r0, r1) in enumerate(bounds):
+            if prev_out[c] is not None:
+                s_in.wait_event(prev_out[-1] if whole and c == 0 else prev_out[c])
             with torch.cuda.stream(s_in):
                 for k in in_keys:
                     sl = rows_of(k, r0, r1)
@@ -279,8 +287,11 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
                             host_out[k].copy_(d[k], non_blocking=True)
                         continue
                     host_out[k][sl].copy_(d[k][sl], non_blocking=True)
-        s_in.wait_stream(s_out)  # next step's inputs overwrite after readback
-        s_cmp.wait_stream(s_out)
+                ev = torch.cuda.Event()
+                ev.record(s_out)
+                prev_out[c] = ev
+        # (the next step's compute of a chunk waits for its uploads, which
+        # wait for this step's readback of the chunk)
 
     for _ in range(2):
         one_step()
