@@ -209,31 +209,40 @@ __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
   }
 }
 
-// Lane-per-position form of the slice kernel (head_dim 64 or 128): each
-// warp takes its slice's positions 32 at a time, stages those 32 K rows in
-// shared memory (cp.async, rows padded by 16 bytes so that a lane reading
-// its own row stays on distinct banks), and lane l scores position
-// block + l against all G query heads with plain FMAs — no cross-lane
-// reduction per dot product.  One warp max / sum per block and head feeds
-// the online softmax; P.V then walks the block's positions with the
-// probabilities broadcast by shuffles and each lane accumulating DPL = hd / 32
-// dimensions of a coalesced V row.  The 4 warps' states are merged and
-// written as the slice partial, as in AttnPartialKernel.
-constexpr int kLaneBlock = 32;
+// Position-parallel form of the slice kernel (head_dim 64 or 128): each
+// warp takes its slice's positions 16 at a time and stages those 16 K and V
+// rows in shared memory with cp.async (one wait per block, so every warp has
+// a whole block of loads in flight; ~17 KB per warp lets 3 CTAs share an
+// SM).  Lanes 2r and 2r + 1 score position block + r against all G query
+// heads, each over one half of the dimensions, and add their halves with one
+// shuffle — instead of a 5-shuffle reduction per dot product.  K rows are
+// padded and their second half stored with chunk index ^ 4, so the two
+// lanes of a position (and the 4 positions of a quarter-warp) read distinct
+// banks.  One warp max / sum per block and head feeds the online softmax;
+// P.V walks the block's positions with the probabilities broadcast by
+// shuffles and each lane accumulating DPL = hd / 32 dimensions of a V row
+// read from shared memory.  The 4 warps' states are merged and written as
+// the slice partial, as in AttnPartialKernel.
+constexpr int kLaneBlock = 16;
 
 template <int HD4>
-__host__ __device__ constexpr int LaneRowFloats() { return 4 * HD4 + 4; }
+__host__ __device__ constexpr int LaneKRowFloats() { return 4 * HD4 + 4; }
+template <int HD4>
+__host__ __device__ constexpr int LaneWarpFloats() {  // K block + V block
+  return kLaneBlock * (LaneKRowFloats<HD4>() + 4 * HD4);
+}
 
 template <int G, int HD4>
 __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArgs a) {
   constexpr int HD = 4 * HD4;
   constexpr int DPL = HD / 32;        // dimensions per lane in P.V (2 or 4)
-  constexpr int RF = LaneRowFloats<HD4>();
-  // dynamic: q of the G heads, then per warp a staged block of K rows (the
-  // warps' final accumulators reuse the K area once the loop is done)
+  constexpr int KRF = LaneKRowFloats<HD4>();
+  constexpr int HALF4 = HD4 / 2;      // float4 chunks per half row
+  // dynamic: q of the G heads, then per warp a staged block of K and V rows
+  // (the warps' final accumulators reuse that area once the loop is done)
   extern __shared__ __align__(16) float lsm[];
   float* qs = lsm;                   // [G][HD]
-  float* ks_all = lsm + G * HD;      // [kAttnWarps][kLaneBlock][RF]
+  float* blk_all = lsm + G * HD;     // [kAttnWarps][K rows | V rows]
   __shared__ float sm_m[kAttnWarps][G];
   __shared__ float sm_l[kAttnWarps][G];
   const int lane = threadIdx.x & 31;
@@ -254,6 +263,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
         __ldg(reinterpret_cast<const float4*>(q_row + static_cast<int64_t>(g) * G * HD) + i);
   __syncthreads();
 
+  const int pos = lane >> 1;  // position of this lane pair in the block
+  const int half = lane & 1;  // which half of the dimensions it scores
   float m[G], l[G], acc[G][DPL];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -262,30 +273,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
 #pragma unroll
     for (int e = 0; e < DPL; ++e) acc[h][e] = 0.0f;
   }
-  float* kw = ks_all + warp * kLaneBlock * RF;
+  float* kw = blk_all + warp * LaneWarpFloats<HD4>();
+  float* vw = kw + kLaneBlock * KRF;
   for (int64_t blk = t_begin + static_cast<int64_t>(warp) * kLaneBlock; blk < t_end;
        blk += kAttnWarps * kLaneBlock) {
     const int n = static_cast<int>(t_end - blk < kLaneBlock ? t_end - blk : kLaneBlock);
-    // stage K rows blk .. blk + n - 1 (coalesced: lane l copies float4 l, l + 32, ...)
+    // stage K and V rows blk .. blk + n - 1 (coalesced); K chunk c of the
+    // second half goes to c ^ 4
     for (int i = lane; i < n * HD4; i += 32) {
       const int r = i / HD4, c = i - r * HD4;
-      CopyAsync16(kw + r * RF + 4 * c, kbase + (blk + r) * kv_stride + 4 * c);
+      const int64_t off = (blk + r) * kv_stride + 4 * c;
+      CopyAsync16(kw + r * KRF + 4 * (c >= HALF4 ? (c ^ 4) : c), kbase + off);
+      CopyAsync16(vw + r * HD + 4 * c, vbase + off);
     }
     CopyAsyncCommit();
     CopyAsyncWait<0>();
     __syncwarp();
-    // scores of position blk + lane for the G heads
+    // half scores of position blk + pos
     float sc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) sc[h] = 0.0f;
-    if (lane < n) {
-      const float* kr = kw + lane * RF;
+    if (pos < n) {
+      const float* kr = kw + pos * KRF;
 #pragma unroll 8
-      for (int c = 0; c < HD4; ++c) {
-        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * c);
+      for (int c = 0; c < HALF4; ++c) {
+        const int cc = half * HALF4 + c;  // logical chunk
+        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * (half ? (cc ^ 4) : cc));
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float4 qv = *reinterpret_cast<const float4*>(qs + h * HD + 4 * c);
+          const float4 qv = *reinterpret_cast<const float4*>(qs + h * HD + 4 * cc);
           sc[h] = fmaf(qv.x, kv.x, sc[h]);
           sc[h] = fmaf(qv.y, kv.y, sc[h]);
           sc[h] = fmaf(qv.z, kv.z, sc[h]);
@@ -296,38 +312,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
     float p[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      const float score = lane < n ? __fmul_rn(sc[h], a.scale) : -INFINITY;
+      const float dot = sc[h] + __shfl_xor_sync(0xffffffffu, sc[h], 1);
+      const float score = pos < n ? __fmul_rn(dot, a.scale) : -INFINITY;
       const float m_new = fmaxf(m[h], WarpMax(score));
       const float alpha = expf(m[h] - m_new);  // 0 on the first block
-      p[h] = lane < n ? expf(score - m_new) : 0.0f;
-      l[h] = fmaf(l[h], alpha, WarpSum(p[h]));
+      p[h] = pos < n ? expf(score - m_new) : 0.0f;
+      // each position's p sits on both lanes of its pair: count it once
+      l[h] = fmaf(l[h], alpha, WarpSum(half ? 0.0f : p[h]));
       m[h] = m_new;
 #pragma unroll
       for (int e = 0; e < DPL; ++e) acc[h][e] *= alpha;
     }
     // P.V over the block's positions (V row r: lane owns dims DPL * lane ..)
     for (int r = 0; r < n; ++r) {
-      const float* vr = vbase + (blk + r) * kv_stride + DPL * lane;
+      const float* vr = vw + r * HD + DPL * lane;
       float v[DPL];
       if (DPL == 4) {
-        const float4 x = __ldg(reinterpret_cast<const float4*>(vr));
+        const float4 x = *reinterpret_cast<const float4*>(vr);
         v[0] = x.x; v[1] = x.y; v[2 % DPL] = x.z; v[3 % DPL] = x.w;
       } else {
-        const float2 x = __ldg(reinterpret_cast<const float2*>(vr));
+        const float2 x = *reinterpret_cast<const float2*>(vr);
         v[0] = x.x; v[1] = x.y;
       }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float pr = __shfl_sync(0xffffffffu, p[h], r);
+        const float pr = __shfl_sync(0xffffffffu, p[h], 2 * r);
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(pr, v[e], acc[h][e]);
       }
     }
-    __syncwarp();  // every lane is done with kw before it is restaged
+    __syncwarp();  // every lane is done with this block before it is restaged
   }
   // merge the 4 warps, then write the slice partial
-  __syncthreads();  // every warp is done with its K rows: reuse them
-  float* sm_acc = ks_all;  // [kAttnWarps][G][HD]
+  __syncthreads();  // every warp is done with its rows: reuse the area
+  float* sm_acc = blk_all;  // [kAttnWarps][G][HD]
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     if (lane == 0) {
@@ -364,7 +382,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
 
 template <int G, int HD4>
 int LaunchLane(const AttnArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr size_t kStage = static_cast<size_t>(kAttnWarps) * kLaneBlock * LaneRowFloats<HD4>();
+  constexpr size_t kStage = static_cast<size_t>(kAttnWarps) * LaneWarpFloats<HD4>();
   constexpr size_t kAcc = static_cast<size_t>(kAttnWarps) * G * 4 * HD4;
   constexpr size_t shm = sizeof(float) * (G * 4 * HD4 + (kStage > kAcc ? kStage : kAcc));
   auto kernel = AttnLanePartialKernel<G, HD4>;
