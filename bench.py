@@ -670,6 +670,8 @@ def linear_bench(args):
         if args.linear_shapes else LINEAR_SHAPES
     tokens = [int(t) for t in args.linear_tokens.split(",")] \
         if args.linear_tokens else (1, 4, 8)
+    mlb.set_gemv_path(args.gemv_path)
+    path_name = {0: "gemv", 1: "gemv cuda-core", 2: "gemv int8 tensor-core"}[args.gemv_path]
     for qt in qts:
         for n, k in shapes:
             w = wl.quant_table(qt, n, k, dev, seed=1)
@@ -689,7 +691,7 @@ def linear_bench(args):
                 gbs = nbytes / (ms / 1e3) / 1e9
                 line = {
                     "linear": wl.QNAME[qt], "n": n, "k": k, "tokens": t,
-                    "path": "tcgen05 tf32x3" if tc else "gemv",
+                    "path": "tcgen05 tf32x3" if tc else path_name,
                     "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
                     "frac_of_measured": round(gbs / peak, 4),
                     "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
@@ -943,6 +945,9 @@ def main():
     ap.add_argument("--linear-qtypes", default="", help="e.g. Q8_0,F32")
     ap.add_argument("--linear-shapes", default="", help="e.g. 14336x4096")
     ap.add_argument("--linear-tokens", default="", help="e.g. 1,4")
+    ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1, 2),
+                    help="decode linear kernel: 0 automatic, 1 CUDA-core GEMV, "
+                         "2 int8 tensor-core GEMV where allowed")
     ap.add_argument("--sweep-ops", default="")
     ap.add_argument("--sweep-hidden", default="")
     ap.add_argument("--sweep-tokens", default="")

@@ -200,9 +200,24 @@ int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
  * within |y - y_ref| <= 1e-5 * sum_i |w_i x_i|.  Weights are read once per
  * group of 8 tokens; k % 32 != 0 or unaligned x take a scalar path that keeps
  * the reference's summation order.
+ * Wide ggml matrices (Q8_0: k % 256 == 0, Q4_0 / Q4_1: k % 512 == 0,
+ * k <= 4096, 16-byte aligned table) run on the int8 tensor cores instead,
+ * up to 4 tokens per pass: the codes enter the MMA as stored and x as four
+ * exact int8 digits per value relative to a power-of-two block scale
+ * (|x_i - digits| <= 2^-27 max|x| of its block), within the same bound.
  */
 int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                    const float* x, int64_t t_rows, float* y, void* stream);
+
+/*
+ * Kernel choice of mlb_linear_f32 for ggml formats: 0 = automatic (the
+ * default), 1 = always the CUDA-core GEMV, 2 = the tensor-core GEMV wherever
+ * its shape rules allow.  Process-wide; for benchmarks and tests.  Returns
+ * MLB_OK, or MLB_ERR_ARG for another value.  mlb_gemv_path returns the
+ * current setting.  No counterpart in the reference.
+ */
+int mlb_set_gemv_path(int path);
+int mlb_gemv_path(void);
 
 /* Floats of scratch mlb_linear_rows_f32 needs for t_rows tokens of k values
  * (-1 for bad arguments). */

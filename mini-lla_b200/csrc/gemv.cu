@@ -662,14 +662,36 @@ int LaunchVec(const GemvArgs& a, int t_rows, bool bulk_ok, cudaStream_t s) {
 
 namespace mlb {
 unsigned int TcWaitTimeouts();  // linear_tc.cu
+// gemv_tc.cu
+int GemvTcSplit(int qtype, const void* w, int64_t n, int64_t k, int tokens);
+int GemvTc(int qtype, const void* w, int64_t n, int64_t k, const float* x, int tokens,
+           float* y, int split, cudaStream_t s);
+unsigned int GemvTcWaitTimeouts();
 }  // namespace mlb
+
+namespace {
+// mlb_set_gemv_path: 0 automatic, 1 CUDA cores only, 2 tensor cores where allowed
+int g_gemv_path = 0;
+// Automatic choice: the tensor-core GEMV (one CTA per 128-row tile) once
+// the rows fill this many tiles.
+constexpr int64_t kGemvTcMinTiles = 64;
+constexpr int kGemvTcTokens = 4;  // tokens per tensor-core pass
+}  // namespace
+
+extern "C" int mlb_set_gemv_path(int path) {
+  if (path < 0 || path > 2) return mlb::Fail(MLB_ERR_ARG, "mlb_set_gemv_path: bad path");
+  g_gemv_path = path;
+  return MLB_OK;
+}
+
+extern "C" int mlb_gemv_path(void) { return g_gemv_path; }
 
 extern "C" int mlb_wait_timeouts(unsigned int* count) {
   using namespace mlb;
   if (count == nullptr) return Fail(MLB_ERR_ARG, "mlb_wait_timeouts: null pointer");
   if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
-  *count += TcWaitTimeouts();
+  *count += TcWaitTimeouts() + GemvTcWaitTimeouts();
   return MLB_OK;
 }
 
@@ -699,6 +721,19 @@ extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
     GemvScalarKernel<<<static_cast<unsigned>(blocks < 65535 * 64 ? blocks : 65535 * 64),
                        256, 0, s>>>(a, qtype, t_rows);
     return CheckLaunch("mlb_linear_f32");
+  }
+  // wide ggml matrices: int8 tensor cores, kGemvTcTokens tokens per pass
+  const int first = static_cast<int>(t_rows < kGemvTcTokens ? t_rows : kGemvTcTokens);
+  if (g_gemv_path != 1 && GemvTcSplit(qtype, w, n, k, first) > 0 &&
+      (g_gemv_path == 2 || (n + 127) / 128 >= kGemvTcMinTiles)) {
+    for (int64_t t0 = 0; t0 < t_rows; t0 += kGemvTcTokens) {
+      const int tg = static_cast<int>(t_rows - t0 < kGemvTcTokens ? t_rows - t0 : kGemvTcTokens);
+      const int split = GemvTcSplit(qtype, w, n, k, tg);
+      if (split <= 0) return Fail(MLB_ERR_ARG, "mlb_linear_f32: no tensor-core split");
+      const int rc = GemvTc(qtype, w, n, k, x + t0 * k, tg, y + t0 * n, split, s);
+      if (rc != MLB_OK) return rc;
+    }
+    return MLB_OK;
   }
   // bulk copies need a 16-byte aligned table (segments start on 8-block,
   // i.e. 16-byte, boundaries of it)

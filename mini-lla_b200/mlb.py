@@ -51,6 +51,8 @@ SIGNATURES = {
                                      c_void_p]),
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
     "mlb_wait_timeouts": (c_int, [c_void_p]),
+    "mlb_set_gemv_path": (c_int, [c_int]),
+    "mlb_gemv_path": (c_int, []),
     "mlb_linear_rows_scratch_floats": (c_int64, [c_int64, c_int64]),
     "mlb_linear_rows_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                     c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
@@ -466,6 +468,15 @@ def status_check(status, stream=None) -> int:
     if rc not in (0, 3):
         _check(rc, "status_check")
     return bits.value
+
+
+def set_gemv_path(path: int) -> int:
+    """Kernel choice of linear() for ggml formats: 0 automatic, 1 CUDA-core
+    GEMV, 2 int8 tensor-core GEMV wherever its shape rules allow.  Returns
+    the previous setting."""
+    previous = load().mlb_gemv_path()
+    _check(load().mlb_set_gemv_path(int(path)), "set_gemv_path")
+    return previous
 
 
 def wait_timeouts() -> int:

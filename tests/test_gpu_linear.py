@@ -141,3 +141,91 @@ def test_linear_rows_group_vs_single(cuda, oracle, qtype, t):
         want = oracle.linear(tb, qtype, n, k, x)
         wdeq, _ = oracle.embedding(tb, qtype, n, k, np.arange(n, dtype=np.int32))
         _check(got.cpu().numpy(), want, wdeq, x, f"group {wl.QNAME[qtype]} n={n} t={t}")
+
+
+@pytest.fixture
+def tensor_core_gemv():
+    """Forces mlb.linear onto the int8 tensor-core GEMV wherever its shape
+    rules allow (restores the automatic choice afterwards)."""
+    previous = mlb.set_gemv_path(2)
+    yield
+    mlb.set_gemv_path(previous)
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0, wl.Q4_1])
+@pytest.mark.parametrize("n,k,t", [(37, 512, 1), (300, 4096, 1), (129, 1024, 3),
+                                   (256, 2048, 4), (200, 4096, 5), (1000, 512, 8),
+                                   (128, 4096, 2), (64, 256, 1), (256, 14336, 1),
+                                   (300, 7168, 2), (5000, 1536, 1)])
+def test_linear_tensor_core_gemv_vs_oracle(cuda, oracle, tensor_core_gemv, qtype, n, k, t):
+    """int8 tensor-core GEMV (codes as stored, x as exact int8 digits):
+    ragged tiles, 1..8 tokens (passes of 4), every ggml format, k split
+    over clusters of 1..8 CTAs (evenly and unevenly)."""
+    import torch
+    rng = np.random.default_rng(n * 5 + k + t + qtype)
+    table = wl.numpy_quant_table(qtype, n, k, seed=n + 3 * k)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"tc {wl.QNAME[qtype]} n={n} k={k} t={t}")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0, wl.Q4_1])
+def test_linear_tensor_core_gemv_x_ranges(cuda, oracle, tensor_core_gemv, qtype):
+    """Blocks of x that are all zero, tiny (1e-30), huge (1e30), or spread
+    over three decades inside one block; a NaN in a block of x makes every
+    output of that token NaN, as in the reference's sum."""
+    import torch
+    n, k = 384, 1024
+    rng = np.random.default_rng(qtype + 40)
+    table = wl.numpy_quant_table(qtype, n, k, seed=77)
+    x = rng.standard_normal((4, k), dtype=np.float32)
+    x[0, 0:32] = 0.0
+    x[0, 64:96] *= np.float32(1e-30)
+    x[1, 128:160] *= np.float32(1e30)
+    x[2] *= (10.0 ** rng.uniform(-1.5, 1.5, k)).astype(np.float32)
+    x[3, 0:32] = 0.0
+    x[3, 32:64] *= np.float32(1e-30)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"tc ranges {wl.QNAME[qtype]}")
+    xn = x.copy()
+    xn[1, 300] = np.nan
+    got = mlb.linear(dev(table, cuda), qtype, n, k, dev(xn, cuda)).cpu().numpy()
+    assert np.isnan(got[1]).all()
+    for t in (0, 2, 3):
+        assert np.isfinite(got[t]).all()
+
+
+def test_linear_tensor_core_gemv_deterministic_and_auto(cuda, oracle):
+    """The automatic choice takes the tensor-core GEMV for a wide matrix
+    (LLaMA-3-8B FFN up, 14336 x 4096 Q8_0); repeated calls give identical
+    bits and agree with the CUDA-core GEMV within the bound."""
+    import torch
+    n, k = 14336, 4096
+    rng = np.random.default_rng(9)
+    table_d = wl.quant_table(wl.Q8_0, n, k, cuda, seed=5)
+    x = dev(rng.standard_normal((2, k), dtype=np.float32), cuda)
+    a = mlb.linear(table_d, wl.Q8_0, n, k, x)
+    b = mlb.linear(table_d, wl.Q8_0, n, k, x)
+    previous = mlb.set_gemv_path(1)
+    try:
+        c = mlb.linear(table_d, wl.Q8_0, n, k, x)
+    finally:
+        mlb.set_gemv_path(previous)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    rows = np.unique(np.r_[0, n - 1, rng.integers(0, n, 200)])
+    rb = wl.row_bytes(wl.Q8_0, k)
+    tbl = table_d.view(n, rb)[torch.from_numpy(rows).to(cuda)].cpu().numpy()
+    xs = x.cpu().numpy()
+    want = oracle.linear(tbl.reshape(-1), wl.Q8_0, rows.size, k, xs)
+    wdeq, _ = oracle.embedding(tbl.reshape(-1), wl.Q8_0, rows.size, k,
+                               np.arange(rows.size, dtype=np.int32))
+    _check(a.cpu().numpy()[:, rows], want, wdeq, xs, "auto tensor-core 14336x4096")
+    _check(c.cpu().numpy()[:, rows], want, wdeq, xs, "cuda-core 14336x4096")
