@@ -463,3 +463,26 @@ def test_embedding_last_row_at_unaligned_table_end(cuda, oracle, qtype):
         got = mlb.embedding_rows(dev(table, cuda), qtype, vocab, cols,
                                  dev(tokens, cuda))
         assert_bitexact(host(got), want, f"{wl.QNAME[qtype]} vocab={vocab}")
+
+
+@pytest.mark.parametrize("qtype,cols", [(wl.Q8_0, 2432), (wl.Q8_0, 4096), (wl.Q4_0, 8192),
+                                        (wl.Q4_1, 8192)])
+def test_embedding_large_batch_pipelined(cuda, oracle, qtype, cols):
+    """Large batches of long rows take the persistent double-buffered
+    gather: every row bit-exact, out-of-range ids zeroed and flagged, and the
+    last row of a table whose size is not a multiple of 16 bytes."""
+    import torch
+    rng = np.random.default_rng(cols + qtype)
+    vocab, T = 5, 3000
+    table = wl.numpy_quant_table(qtype, vocab, cols, seed=cols)
+    tokens = rng.integers(0, vocab, T).astype(np.int32)
+    tokens[-1] = vocab - 1
+    tokens[[7, 1500]] = [-1, vocab]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = host(mlb.embedding_rows(dev(table, cuda), qtype, vocab, cols, dev(tokens, cuda),
+                                  status=status))
+    ok = (tokens >= 0) & (tokens < vocab)
+    want, _ = oracle.embedding(table, qtype, vocab, cols, tokens[ok])
+    assert_bitexact(got[ok], want, f"{wl.QNAME[qtype]} cols={cols}")
+    assert (got[~ok] == 0).all()
+    assert int(status.item()) & mlb.STATUS_BAD_TOKEN
