@@ -467,10 +467,10 @@ def test_embedding_last_row_at_unaligned_table_end(cuda, oracle, qtype):
 
 @pytest.mark.parametrize("qtype,cols", [(wl.Q8_0, 2432), (wl.Q8_0, 4096), (wl.Q4_0, 8192),
                                         (wl.Q4_1, 8192)])
-def test_embedding_large_batch_pipelined(cuda, oracle, qtype, cols):
-    """Large batches of long rows take the persistent double-buffered
-    gather: every row bit-exact, out-of-range ids zeroed and flagged, and the
-    last row of a table whose size is not a multiple of 16 bytes."""
+def test_embedding_large_batch_long_rows(cuda, oracle, qtype, cols):
+    """Large batches of long rows (the staged one-row-per-CTA gather): every
+    row bit-exact, out-of-range ids zeroed and flagged, and the last row of a
+    table whose size is not a multiple of 16 bytes."""
     import torch
     rng = np.random.default_rng(cols + qtype)
     vocab, T = 5, 3000
