@@ -663,20 +663,47 @@ int LaunchVec(const GemvArgs& a, int t_rows, bool bulk_ok, cudaStream_t s) {
 namespace mlb {
 unsigned int TcWaitTimeouts();  // linear_tc.cu
 // gemv_tc.cu
-int GemvTcSplit(int qtype, const void* w, int64_t n, int64_t k, int tokens);
-int GemvTc(int qtype, const void* w, int64_t n, int64_t k, const float* x, int tokens,
-           float* y, int split, cudaStream_t s);
+int GemvTcSplit(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
+                int tokens);
+int64_t GemvTcTiles(int count, const int64_t* n);
+int GemvTc(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
+           const float* x, int tokens, float* const* y, int split, cudaStream_t s);
 unsigned int GemvTcWaitTimeouts();
 }  // namespace mlb
 
 namespace {
 // mlb_set_gemv_path: 0 automatic, 1 CUDA cores only, 2 tensor cores where allowed
 int g_gemv_path = 0;
-// Automatic choice: the tensor-core GEMV (one CTA per 128-row tile) once
-// the rows fill this many tiles.
-constexpr int64_t kGemvTcMinTiles = 64;
+// Automatic choice: the tensor-core GEMV once the launch's matrices fill
+// this many 128-row tiles (B200, T = 1: 4096 x 4096 alone 16.4 us against
+// 14.4 us on the CUDA cores; q / k / v of LLaMA-3-8B together, 48 tiles, and
+// every wider matrix gain).
+constexpr int64_t kGemvTcMinTiles = 40;
 constexpr int kGemvTcTokens = 4;  // tokens per tensor-core pass
 }  // namespace
+
+namespace mlb {
+// W[m] . x[t] for m < count, t < t_rows (< 48) on the int8 tensor cores,
+// one launch per 4 tokens for all matrices, when they qualify; returns -1
+// (nothing launched) when the caller should take the CUDA-core GEMV.
+int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, int64_t k,
+                const float* x, int64_t t_rows, float* const* y, cudaStream_t s) {
+  if (g_gemv_path == 1 || t_rows < 1 || !Aligned16(x)) return -1;
+  const int first = static_cast<int>(t_rows < kGemvTcTokens ? t_rows : kGemvTcTokens);
+  if (GemvTcSplit(qtype, count, w, n, k, first) <= 0) return -1;
+  if (g_gemv_path != 2 && GemvTcTiles(count, n) < kGemvTcMinTiles) return -1;
+  float* yy[3];
+  for (int64_t t0 = 0; t0 < t_rows; t0 += kGemvTcTokens) {
+    const int tg = static_cast<int>(t_rows - t0 < kGemvTcTokens ? t_rows - t0 : kGemvTcTokens);
+    const int split = GemvTcSplit(qtype, count, w, n, k, tg);
+    if (split <= 0) return Fail(MLB_ERR_ARG, "mlb_linear_f32: no tensor-core split");
+    for (int m = 0; m < count; ++m) yy[m] = y[m] + t0 * n[m];
+    const int rc = GemvTc(qtype, count, w, n, k, x + t0 * k, tg, yy, split, s);
+    if (rc != MLB_OK) return rc;
+  }
+  return MLB_OK;
+}
+}  // namespace mlb
 
 extern "C" int mlb_set_gemv_path(int path) {
   if (path < 0 || path > 2) return mlb::Fail(MLB_ERR_ARG, "mlb_set_gemv_path: bad path");
@@ -723,17 +750,9 @@ extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
     return CheckLaunch("mlb_linear_f32");
   }
   // wide ggml matrices: int8 tensor cores, kGemvTcTokens tokens per pass
-  const int first = static_cast<int>(t_rows < kGemvTcTokens ? t_rows : kGemvTcTokens);
-  if (g_gemv_path != 1 && GemvTcSplit(qtype, w, n, k, first) > 0 &&
-      (g_gemv_path == 2 || (n + 127) / 128 >= kGemvTcMinTiles)) {
-    for (int64_t t0 = 0; t0 < t_rows; t0 += kGemvTcTokens) {
-      const int tg = static_cast<int>(t_rows - t0 < kGemvTcTokens ? t_rows - t0 : kGemvTcTokens);
-      const int split = GemvTcSplit(qtype, w, n, k, tg);
-      if (split <= 0) return Fail(MLB_ERR_ARG, "mlb_linear_f32: no tensor-core split");
-      const int rc = GemvTc(qtype, w, n, k, x + t0 * k, tg, y + t0 * n, split, s);
-      if (rc != MLB_OK) return rc;
-    }
-    return MLB_OK;
+  {
+    const int rc = GemvTcGroup(1, &w, qtype, &n, k, x, t_rows, &y, s);
+    if (rc != -1) return rc;
   }
   // bulk copies need a 16-byte aligned table (segments start on 8-block,
   // i.e. 16-byte, boundaries of it)

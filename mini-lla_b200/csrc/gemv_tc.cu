@@ -315,17 +315,31 @@ __device__ __forceinline__ void GtReadChunkAt(int pos, const uint8_t* stage, int
   }
 }
 
+// Up to kGtMaxGroup matrices of one format and width applied to the same x
+// in one launch (the q / k / v projections, the FFN gate / up): their
+// 128-row tiles are numbered matrix by matrix.
+constexpr int kGtMaxGroup = 3;
+
 struct GtArgs {
-  CUtensorMap w;     // raw weight bytes [n, row_bytes]
+  CUtensorMap w[kGtMaxGroup];  // raw weight bytes [n, row_bytes] of each matrix
+  float* y[kGtMaxGroup];       // [tokens, n] each
+  int n[kGtMaxGroup];
+  int tile_begin[kGtMaxGroup + 1];  // first tile of each matrix; [count] = all tiles
+  int count;
   const float* x;    // [tokens, k]
-  float* y;          // [tokens, n]
-  int n;
   int k;
   int tokens;        // <= kGtMaxTokens
   int tiles;
   int split;         // CTAs per cluster: each takes 1 / split of k
   int nbl;           // most blocks of one rank's share of a row
 };
+
+// Matrix of global tile `tile` (tiles are numbered matrix by matrix).
+__device__ __forceinline__ int GtMatrixOf(const GtArgs& a, int tile) {
+  int mat = 0;
+  while (mat + 1 < a.count && tile >= a.tile_begin[mat + 1]) ++mat;
+  return mat;
+}
 
 __device__ __forceinline__ uint32_t GtMapRank(uint32_t addr, uint32_t rank) {
   uint32_t r;
@@ -540,10 +554,12 @@ __global__ void __launch_bounds__(kGtThreads, 1) GemvTcKernel(const __grid_const
           break;
         }
         const int x0 = (s0 + g % spt) * SB * GtBlockBytes(QT);
+        const int tile = tile_of(g / spt);
+        const int mat = GtMatrixOf(a, tile);
         GtExpectTx(raw_full(st), kGtStageBytes);
         for (int b = 0; b < kGtBoxes; ++b)
-          GtTmaLoad(GtSmem(raw + st * kGtStageBytes + b * kGtBoxBytes), &a.w, x0 + kGtBox * b,
-                    tile_of(g / spt) * kGtRows, raw_full(st));
+          GtTmaLoad(GtSmem(raw + st * kGtStageBytes + b * kGtBoxBytes), &a.w[mat],
+                    x0 + kGtBox * b, (tile - a.tile_begin[mat]) * kGtRows, raw_full(st));
         issued = g + 1;
       }
     }
@@ -712,9 +728,12 @@ __global__ void __launch_bounds__(kGtThreads, 1) GemvTcKernel(const __grid_const
               for (int q = 1; q < split; ++q)
                 GtArriveRemote(GtMapRank(red_empty(p), static_cast<uint32_t>(q)));
             }
-            const int row = tile_of(tile_iter) * kGtRows + m;
-            if (row < a.n) {
-              for (int t = 0; t < a.tokens; ++t) a.y[static_cast<int64_t>(t) * a.n + row] = tot[t];
+            const int tile = tile_of(tile_iter);
+            const int mat = GtMatrixOf(a, tile);
+            const int n = a.n[mat];
+            const int row = (tile - a.tile_begin[mat]) * kGtRows + m;
+            if (row < n) {
+              for (int t = 0; t < a.tokens; ++t) a.y[mat][static_cast<int64_t>(t) * n + row] = tot[t];
             }
           }
 #pragma unroll
@@ -739,10 +758,13 @@ __global__ void __launch_bounds__(kGtThreads, 1) GemvTcKernel(const __grid_const
     }
     if (warp < 4) {
       for (int ti = 0; ti < my_tiles; ++ti) {
-        const int row = tile_of(ti) * kGtRows + static_cast<int>(threadIdx.x);
-        if (row < a.n)
+        const int tile = tile_of(ti);
+        const int mat = GtMatrixOf(a, tile);
+        const int n = a.n[mat];
+        const int row = (tile - a.tile_begin[mat]) * kGtRows + static_cast<int>(threadIdx.x);
+        if (row < n)
           for (int t = 0; t < a.tokens; ++t)
-            a.y[static_cast<int64_t>(t) * a.n + row] = __int_as_float(0x7fc00000);
+            a.y[mat][static_cast<int64_t>(t) * n + row] = __int_as_float(0x7fc00000);
       }
     }
   }
@@ -774,14 +796,13 @@ PFN_cuTensorMapEncodeTiled_v12000 GtEncodeFn() {
   return fn;
 }
 
-// Ranks per tile (1, 2, 4 or 8) for W [n, k]: as many as keep one cluster
-// per tile within one wave of CTAs, each rank with at least one stage, and
-// enough that a rank's digits of x fit in shared memory; 0 when no split
-// works.
-int GtSplit(int qtype, int64_t n, int64_t k, int tokens) {
+// Ranks per tile (1, 2, 4 or 8) for `tiles` 128-row tiles of width k: as
+// many as keep one cluster per tile within one wave of CTAs, each rank with
+// at least one stage, and enough that a rank's digits of x fit in shared
+// memory; 0 when no split works.
+int GtSplit(int qtype, int64_t tiles, int64_t k, int tokens) {
   const int sb = GtStageBlocks(qtype);
   const int64_t spt = k / 32 / sb;
-  const int64_t tiles = (n + kGtRows - 1) / kGtRows;
   const int digit_bytes = GtN(tokens) * 32;  // per block
   int split = 1;
   while (split < 8 && tiles * split * 2 <= SmCount() && spt >= 2 * split) split *= 2;
@@ -795,36 +816,52 @@ int GtSplit(int qtype, int64_t n, int64_t k, int tokens) {
   return split;
 }
 
+int64_t GtTiles(int count, const int64_t* n) {
+  int64_t tiles = 0;
+  for (int m = 0; m < count; ++m) tiles += (n[m] + kGtRows - 1) / kGtRows;
+  return tiles;
+}
+
+int GtTokenClass(int tokens) { return tokens <= 1 ? 1 : (tokens <= 2 ? 2 : 4); }
+
 template <int QT>
-int LaunchGemvTc(const void* w, int64_t n, int64_t k, const float* x, int tokens, float* y,
-                 int split, cudaStream_t s) {
+int LaunchGemvTc(int count, const void* const* w, const int64_t* n, int64_t k, const float* x,
+                 int tokens, float* const* y, int split, cudaStream_t s) {
   GtArgs a{};
   const int64_t row_bytes = mlb_row_bytes(QT, k);
   PFN_cuTensorMapEncodeTiled_v12000 encode = GtEncodeFn();
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(n)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {kGtBox, kGtRows};
-  const cuuint32_t elem[2] = {1, 1};
-  if (encode == nullptr ||
-      encode(&a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box,
-             elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-          CUDA_SUCCESS)
-    return Fail(MLB_ERR_CUDA, "mlb_linear_f32: tensor map encoding failed");
+  if (encode == nullptr) return Fail(MLB_ERR_CUDA, "mlb_linear_f32: tensor map encoding failed");
+  int tiles = 0;
+  for (int m = 0; m < count; ++m) {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes),
+                                static_cast<cuuint64_t>(n[m])};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {kGtBox, kGtRows};
+    const cuuint32_t elem[2] = {1, 1};
+    if (encode(&a.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w[m]), dims, strides,
+               box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return Fail(MLB_ERR_CUDA, "mlb_linear_f32: tensor map encoding failed");
+    a.y[m] = y[m];
+    a.n[m] = static_cast<int>(n[m]);
+    a.tile_begin[m] = tiles;
+    tiles += static_cast<int>((n[m] + kGtRows - 1) / kGtRows);
+  }
+  a.tile_begin[count] = tiles;
+  a.count = count;
   constexpr int sb = GtStageBlocks(QT);
   const int spt = static_cast<int>(k / 32 / sb);
   a.x = x;
-  a.y = y;
-  a.n = static_cast<int>(n);
   a.k = static_cast<int>(k);
   a.tokens = tokens;
-  a.tiles = static_cast<int>((n + kGtRows - 1) / kGtRows);
+  a.tiles = tiles;
   a.split = split;
   a.nbl = (spt + split - 1) / split * sb;
-  const int tcount = tokens == 1 ? 1 : (tokens == 2 ? 2 : 4);
-  const int shm = MakeGtLayout(QT, a.nbl, split, tcount).total + 1024;
-  auto kernel = tokens == 1 ? GemvTcKernel<QT, 1>
-                            : (tokens == 2 ? GemvTcKernel<QT, 2> : GemvTcKernel<QT, 4>);
+  const int tclass = GtTokenClass(tokens);
+  const int shm = MakeGtLayout(QT, a.nbl, split, tclass).total + 1024;
+  auto kernel = tclass == 1 ? GemvTcKernel<QT, 1>
+                            : (tclass == 2 ? GemvTcKernel<QT, 2> : GemvTcKernel<QT, 4>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shm) !=
       cudaSuccess) {
     cudaGetLastError();
@@ -847,14 +884,14 @@ int LaunchGemvTc(const void* w, int64_t n, int64_t k, const float* x, int tokens
   static int resident[3][4] = {};
   int& fit = resident[QT - MLB_Q8_0][split == 1 ? 0 : (split == 2 ? 1 : (split == 4 ? 2 : 3))];
   if (fit <= 0) {
-    int count = 0;
-    if (cudaOccupancyMaxActiveClusters(&count, kernel, &cfg) != cudaSuccess || count < 1) {
+    int found = 0;
+    if (cudaOccupancyMaxActiveClusters(&found, kernel, &cfg) != cudaSuccess || found < 1) {
       cudaGetLastError();
-      count = SmCount() / split > 0 ? SmCount() / split : 1;
+      found = SmCount() / split > 0 ? SmCount() / split : 1;
     }
-    fit = count;
+    fit = found;
   }
-  const int clusters = fit < a.tiles ? fit : a.tiles;
+  const int clusters = fit < tiles ? fit : tiles;
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * split));
   if (cudaLaunchKernelEx(&cfg, kernel, a) != cudaSuccess) {
     cudaGetLastError();
@@ -865,28 +902,35 @@ int LaunchGemvTc(const void* w, int64_t n, int64_t k, const float* x, int tokens
 
 }  // namespace
 
-// Ranks per 128-row tile the tensor-core GEMV would use for W [n, k] of
-// format qtype (1, 2, 4 or 8), or 0 when it does not take the matrix: ggml
-// blocks only, a 16-byte aligned table, whole stages per row, x's digits of
-// a rank's share of k within the shared-memory budget.
-int GemvTcSplit(int qtype, const void* w, int64_t n, int64_t k, int tokens) {
+// Ranks per 128-row tile the tensor-core GEMV would use for the `count`
+// matrices W[m] [n[m], k] of format qtype (1, 2, 4 or 8) with `tokens`
+// tokens per pass, or 0 when it does not take them: ggml blocks only,
+// 16-byte aligned tables, whole stages per row, x's digits of a rank's
+// share of k within the shared-memory budget.
+int GemvTcSplit(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
+                int tokens) {
   if (qtype != MLB_Q8_0 && qtype != MLB_Q4_0 && qtype != MLB_Q4_1) return 0;
-  if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0 || n <= 0 || n > INT_MAX || k > INT_MAX)
-    return 0;
+  if (count < 1 || count > kGtMaxGroup || k > INT_MAX) return 0;
+  for (int m = 0; m < count; ++m)
+    if ((reinterpret_cast<uintptr_t>(w[m]) & 15u) != 0 || n[m] <= 0 || n[m] > INT_MAX) return 0;
   if (k % (32 * GtStageBlocks(qtype)) != 0) return 0;
-  return GtSplit(qtype, n, k, tokens <= 1 ? 1 : (tokens <= 2 ? 2 : 4));
+  const int64_t tiles = GtTiles(count, n);
+  if (tiles > INT_MAX / 2) return 0;
+  return GtSplit(qtype, tiles, k, GtTokenClass(tokens));
 }
 
-// y[t] = W . x[t] for t < tokens (1..4) on the tensor cores, `split` ranks
-// per tile (from GemvTcSplit).
-int GemvTc(int qtype, const void* w, int64_t n, int64_t k, const float* x, int tokens,
-           float* y, int split, cudaStream_t s) {
+int64_t GemvTcTiles(int count, const int64_t* n) { return GtTiles(count, n); }
+
+// y[m][t] = W[m] . x[t] for t < tokens (1..4) and m < count on the tensor
+// cores, `split` ranks per tile (from GemvTcSplit).
+int GemvTc(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
+           const float* x, int tokens, float* const* y, int split, cudaStream_t s) {
   if (tokens < 1 || tokens > kGtMaxTokens)
     return Fail(MLB_ERR_ARG, "mlb_linear_f32: bad token group");
   switch (qtype) {
-    case MLB_Q8_0: return LaunchGemvTc<MLB_Q8_0>(w, n, k, x, tokens, y, split, s);
-    case MLB_Q4_0: return LaunchGemvTc<MLB_Q4_0>(w, n, k, x, tokens, y, split, s);
-    default: return LaunchGemvTc<MLB_Q4_1>(w, n, k, x, tokens, y, split, s);
+    case MLB_Q8_0: return LaunchGemvTc<MLB_Q8_0>(count, w, n, k, x, tokens, y, split, s);
+    case MLB_Q4_0: return LaunchGemvTc<MLB_Q4_0>(count, w, n, k, x, tokens, y, split, s);
+    default: return LaunchGemvTc<MLB_Q4_1>(count, w, n, k, x, tokens, y, split, s);
   }
 }
 

@@ -625,6 +625,11 @@ unsigned int TcWaitTimeouts() {
 // form of mlb_linear_f32 reads every weight once per 8 tokens and wins).
 static constexpr int64_t kTcMinTokens = 48;
 
+namespace mlb {
+int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, int64_t k,
+                const float* x, int64_t t_rows, float* const* y, cudaStream_t s);  // gemv.cu
+}  // namespace mlb
+
 extern "C" int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows) {
   if (k <= 0 || t_rows < 0) return -1;
   return 2 * k * t_rows + 8;  // xh, xl (+ room to align each to 16 bytes)
@@ -652,7 +657,28 @@ int LinearRowsGroup(int count, const void* const* w, int qtype, const int64_t* n
             x != nullptr && Aligned16(x);
   for (int m = 0; m < count; ++m)
     tc = tc && w[m] != nullptr && (reinterpret_cast<uintptr_t>(w[m]) & 15u) == 0;
-  if (!tc) {  // the GEMV form, matrix by matrix
+  if (!tc) {  // the GEMV form: all matrices in one tensor-core launch when
+              // they qualify, else matrix by matrix on the CUDA cores
+    if (t_rows < kTcMinTokens && x != nullptr) {
+      const void* ws[kMaxGroup];
+      int64_t ns[kMaxGroup];
+      float* ys[kMaxGroup];
+      int used = 0;
+      bool ok = true;
+      for (int m = 0; m < count; ++m) {
+        if (n[m] == 0) continue;
+        ok = ok && w[m] != nullptr && y[m] != nullptr;
+        ws[used] = w[m];
+        ns[used] = n[m];
+        ys[used] = y[m];
+        ++used;
+      }
+      if (ok && used == 0) return MLB_OK;
+      if (ok) {
+        const int rc = GemvTcGroup(used, ws, qtype, ns, k, x, t_rows, ys, AsStream(stream));
+        if (rc != -1) return rc;
+      }
+    }
     for (int m = 0; m < count; ++m) {
       if (n[m] == 0) continue;
       const int rc = mlb_linear_f32(w[m], qtype, n[m], k, x, t_rows, y[m], stream);

@@ -229,3 +229,46 @@ def test_linear_tensor_core_gemv_deterministic_and_auto(cuda, oracle):
                                np.arange(rows.size, dtype=np.int32))
     _check(a.cpu().numpy()[:, rows], want, wdeq, xs, "auto tensor-core 14336x4096")
     _check(c.cpu().numpy()[:, rows], want, wdeq, xs, "cuda-core 14336x4096")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0, wl.Q4_1])
+@pytest.mark.parametrize("t", [1, 3, 6])
+def test_linear_rows_group_tensor_core_gemv(cuda, oracle, tensor_core_gemv, qtype, t):
+    """Decode-sized grouped launch on the int8 tensor cores: three matrices
+    of different heights (ragged last tiles) in one launch, tiles numbered
+    matrix by matrix, k split over a cluster; each output within the bar."""
+    import torch
+    rng = np.random.default_rng(3 * t + qtype)
+    k = 2048
+    ns = (512, 130, 257)
+    tables = [wl.numpy_quant_table(qtype, n, k, seed=n + t) for n in ns]
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    outs = mlb.linear_rows_group([dev(tb, cuda) for tb in tables], qtype, list(ns), k,
+                                 dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    for tb, n, got in zip(tables, ns, outs):
+        want = oracle.linear(tb, qtype, n, k, x)
+        wdeq, _ = oracle.embedding(tb, qtype, n, k, np.arange(n, dtype=np.int32))
+        _check(got.cpu().numpy(), want, wdeq, x, f"tc group {wl.QNAME[qtype]} n={n} t={t}")
+
+
+def test_linear_rows_group_tensor_core_persistent(cuda, oracle, tensor_core_gemv):
+    """More tiles than resident CTAs (two 14336-row matrices, the FFN gate /
+    up): persistent clusters walk tiles of both matrices; sampled rows of
+    each output against the oracle."""
+    import torch
+    rng = np.random.default_rng(21)
+    n, k = 14336, 4096
+    tabs = [wl.quant_table(wl.Q8_0, n, k, cuda, seed=s) for s in (3, 4)]
+    x = rng.standard_normal((1, k), dtype=np.float32)
+    outs = mlb.linear_rows_group(tabs, wl.Q8_0, [n, n], k, dev(x, cuda))
+    torch.cuda.synchronize()
+    rows = np.unique(np.r_[0, 127, 128, n - 1, rng.integers(0, n, 100)])
+    rb = wl.row_bytes(wl.Q8_0, k)
+    for tab, got in zip(tabs, outs):
+        tbl = tab.view(n, rb)[torch.from_numpy(rows).to(cuda)].cpu().numpy()
+        want = oracle.linear(tbl.reshape(-1), wl.Q8_0, rows.size, k, x)
+        wdeq, _ = oracle.embedding(tbl.reshape(-1), wl.Q8_0, rows.size, k,
+                                   np.arange(rows.size, dtype=np.int32))
+        _check(got.cpu().numpy()[:, rows], want, wdeq, x, "gate/up group")
