@@ -675,10 +675,14 @@ namespace {
 // mlb_set_gemv_path: 0 automatic, 1 CUDA cores only, 2 tensor cores where allowed
 int g_gemv_path = 0;
 // Automatic choice: the tensor-core GEMV once the launch's matrices fill
-// this many 128-row tiles (B200, T = 1: 4096 x 4096 alone 16.4 us against
-// 14.4 us on the CUDA cores; q / k / v of LLaMA-3-8B together, 48 tiles, and
-// every wider matrix gain).
+// kGemvTcMinTiles 128-row tiles, or kGemvTcMinTilesBatch tiles from
+// kGemvTcBatch tokens on.  (B200, Q8_0: 4096 x 4096 at T = 1 16.4 us against
+// 14.4 us on the CUDA cores, at T = 4 18.4 against 20.5; 4096 x 14336 at
+// T = 4 28.7 against 63.5; 1024 x 4096 at T = 4 16.4 against 12.3; q / k / v
+// of LLaMA-3-8B together, 48 tiles, and every wider matrix gain at T = 1.)
 constexpr int64_t kGemvTcMinTiles = 40;
+constexpr int64_t kGemvTcMinTilesBatch = 16;
+constexpr int64_t kGemvTcBatch = 3;
 constexpr int kGemvTcTokens = 4;  // tokens per tensor-core pass
 }  // namespace
 
@@ -691,7 +695,11 @@ int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, in
   if (g_gemv_path == 1 || t_rows < 1 || !Aligned16(x)) return -1;
   const int first = static_cast<int>(t_rows < kGemvTcTokens ? t_rows : kGemvTcTokens);
   if (GemvTcSplit(qtype, count, w, n, k, first) <= 0) return -1;
-  if (g_gemv_path != 2 && GemvTcTiles(count, n) < kGemvTcMinTiles) return -1;
+  if (g_gemv_path != 2) {
+    const int64_t tiles = GemvTcTiles(count, n);
+    if (tiles < kGemvTcMinTiles && (t_rows < kGemvTcBatch || tiles < kGemvTcMinTilesBatch))
+      return -1;
+  }
   float* yy[3];
   for (int64_t t0 = 0; t0 < t_rows; t0 += kGemvTcTokens) {
     const int tg = static_cast<int>(t_rows - t0 < kGemvTcTokens ? t_rows - t0 : kGemvTcTokens);
