@@ -669,6 +669,7 @@ int64_t GemvTcTiles(int count, const int64_t* n);
 int GemvTc(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
            const float* x, int tokens, float* const* y, int split, cudaStream_t s);
 unsigned int GemvTcWaitTimeouts();
+unsigned int LinearF16WaitTimeouts();  // linear_f16.cu
 }  // namespace mlb
 
 namespace {
@@ -726,7 +727,7 @@ extern "C" int mlb_wait_timeouts(unsigned int* count) {
   if (count == nullptr) return Fail(MLB_ERR_ARG, "mlb_wait_timeouts: null pointer");
   if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
-  *count += TcWaitTimeouts() + GemvTcWaitTimeouts();
+  *count += TcWaitTimeouts() + GemvTcWaitTimeouts() + LinearF16WaitTimeouts();
   return MLB_OK;
 }
 

@@ -628,6 +628,11 @@ static constexpr int64_t kTcMinTokens = 48;
 namespace mlb {
 int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, int64_t k,
                 const float* x, int64_t t_rows, float* const* y, cudaStream_t s);  // gemv.cu
+// linear_f16.cu
+bool LinearF16Eligible(int qtype, int64_t k, int64_t row_bytes);
+int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int64_t k,
+              int64_t row_bytes, const float* x, int64_t t_rows, float* const* y,
+              float* scratch, cudaStream_t s);
 }  // namespace mlb
 
 extern "C" int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows) {
@@ -706,6 +711,9 @@ int LinearRowsGroup(int count, const void* const* w, int qtype, const int64_t* n
   float* xh = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t{15});
   float* xl = xh + k * t_rows;  // k % 32 == 0: still 16-byte aligned
   cudaStream_t s = AsStream(stream);
+  // Q8_0 / Q4_0: the codes are exact fp16 operands (linear_f16.cu)
+  if (LinearF16Eligible(qtype, k, row_bytes))
+    return LinearF16(used, ws, qtype, ns, k, row_bytes, x, t_rows, ys, xh, s);
   const int64_t count4 = k * t_rows / 4;
   SplitTf32Kernel<<<static_cast<unsigned>((count4 + 255) / 256), 256, 0, s>>>(
       reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(xh),
