@@ -652,6 +652,16 @@ LINEAR_TC_MIN_TOKENS = 48   # mlb_linear_rows_f32 runs on the tensor cores from 
 TF32_DENSE_TFLOPS = 1100.0  # B200 nominal dense TF32 (no measured figure in the pool file)
 
 
+def measured_tensor_peak():
+    """Measured dense bf16 TFLOP/s of this pool's B200s (burst; fp16 runs at the
+    same rate), or None."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def linear_bench(args):
     """Decode-path linear layer (mlb_linear_f32): one JSON line per
     (format, n, k, tokens) — LLaMA-3-8B FFN gate/up [14336, 4096] and down
@@ -689,15 +699,24 @@ def linear_bench(args):
                 nbytes = n * wl.row_bytes(qt, k) + 4 * t * (k + n)
                 ms = time_fn(fn, nbytes, 1)
                 gbs = nbytes / (ms / 1e3) / 1e9
+                f16 = tc and qt in (wl.Q8_0, wl.Q4_0) and k % 64 == 0
                 line = {
                     "linear": wl.QNAME[qt], "n": n, "k": k, "tokens": t,
-                    "path": "tcgen05 tf32x3" if tc else path_name,
+                    "path": ("tcgen05 f16, codes exact, x in 2 pieces" if f16 else
+                             "tcgen05 tf32x3") if tc else path_name,
                     "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
                     "frac_of_measured": round(gbs / peak, 4),
                     "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
                     "peak_kind": peak_kind,
                     "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}
-                if tc:  # 3 TF32 products per multiply-add: against the dense TF32 peak
+                if f16:  # 2 fp16 products per multiply-add: against the measured bf16 peak
+                    tflops = 2 * 2 * n * k * t / (ms / 1e3) / 1e12
+                    peak_tf = measured_tensor_peak()
+                    line.update({"f16_tflops": round(tflops, 1),
+                                 "frac_of_tensor_peak": round(tflops / peak_tf, 4)
+                                 if peak_tf else None,
+                                 "fp32_equiv_tflops": round(tflops / 2, 1)})
+                elif tc:  # 3 TF32 products per multiply-add: against the dense TF32 peak
                     tflops = 3 * 2 * n * k * t / (ms / 1e3) / 1e12
                     line.update({"tf32_tflops": round(tflops, 1),
                                  "frac_of_tf32_peak": round(tflops / TF32_DENSE_TFLOPS, 4),
