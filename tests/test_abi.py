@@ -167,3 +167,20 @@ def test_algorithmic_bytes_match_formulas():
     assert c3.bytes_embedding() == 16384 * (128 * 34 + 4 * 4096 + 4)
     c1 = wl.CONFIGS["qwen2-0.5b-t256"]
     assert c1.bytes_softmax() == 4 * 14 * 256 * 257 // 2 + 4 * 14 * 256 * 256
+
+
+def test_gemv_path_switch():
+    """The decode-linear kernel choice (no GPU work): 0 / 1 / 2 are taken and
+    read back, anything else is refused and leaves the setting alone."""
+    lib = mlb.load()
+    previous = lib.mlb_gemv_path()
+    try:
+        for path in (1, 2, 0):
+            assert lib.mlb_set_gemv_path(path) == 0
+            assert lib.mlb_gemv_path() == path
+        for bad in (-1, 3):
+            assert lib.mlb_set_gemv_path(bad) == 1  # MLB_ERR_ARG
+            assert lib.mlb_gemv_path() == 0
+        assert mlb.set_gemv_path(2) == 0 and mlb.set_gemv_path(0) == 2
+    finally:
+        lib.mlb_set_gemv_path(previous)
