@@ -217,15 +217,20 @@ int main(int argc, char** argv) {
 
     // decode steps after the prompt
     double decode_s = 0;
+    float decode_device_ms = 0;
     if (a.decode > 0) {
       const int start = a.tokens;
       for (int i = 0; i < 2; ++i) ForwardBatchCuda(context, model, MiniBatch::Single(tok(rng), start));
       Sync();
       const auto t1 = std::chrono::steady_clock::now();
+      cudaEventRecord(e0, nullptr);
       for (int i = 0; i < a.decode && start + i < a.max_seq; ++i)
         ForwardBatchCuda(context, model, MiniBatch::Single(tok(rng), start + i));
+      cudaEventRecord(e1, nullptr);
       Sync();
       decode_s = Seconds(t1) / a.decode;
+      cudaEventElapsedTime(&decode_device_ms, e0, e1);
+      decode_device_ms /= a.decode;
     }
 
     // the reference's per-token GPU driver (ForwardBatch -> ForwardTokenCuda)
@@ -259,12 +264,13 @@ int main(int argc, char** argv) {
         "{\"model\": {\"vocab\": %d, \"dim\": %d, \"hidden\": %d, \"layers\": %d, "
         "\"heads\": %d, \"kv_heads\": %d, \"type\": \"%s\"}, \"prompt_tokens\": %d, "
         "\"prefill_ms\": %.3f, \"prefill_device_ms\": %.3f, \"prefill_tokens_per_s\": %.1f, "
-        "\"decode_ms_per_token\": %.4f, \"per_token_driver_ms_per_token\": %.4f, "
+        "\"decode_ms_per_token\": %.4f, \"decode_device_ms_per_token\": %.4f, "
+        "\"per_token_driver_ms_per_token\": %.4f, "
         "\"cpu_ms_per_token\": %.2f, \"cpu_threads\": %u, \"cpu_tokens\": %d, "
         "\"per_token_tokens\": %d}\n",
         a.vocab, a.dim, a.hidden, a.layers, a.heads, a.kv_heads, TypeName(a.type),
         a.tokens, prefill_s * 1e3, device_ms, a.tokens / prefill_s, decode_s * 1e3,
-        per_token_s * 1e3, cpu_s * 1e3, cores, a.cpu_tokens, std::min(a.per_token, a.tokens));
+        decode_device_ms, per_token_s * 1e3, cpu_s * 1e3, cores, a.cpu_tokens, std::min(a.per_token, a.tokens));
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());
     return 1;
