@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
   extern __shared__ __align__(16) float lsm[];
   float* qs = lsm;                   // [G][HD]
   float* blk_all = lsm + G * HD;     // [kAttnWarps][K rows | V rows]
+  __shared__ __align__(16) float sm_p[kAttnWarps][kLaneBlock][G];  // a block's probabilities
   __shared__ float sm_m[kAttnWarps][G];
   __shared__ float sm_l[kAttnWarps][G];
   const int lane = threadIdx.x & 31;
@@ -309,20 +310,45 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
         }
       }
     }
-    float p[G];
+    // online softmax of the block, the G heads' warp reductions interleaved
+    // (same butterfly order as WarpMax / WarpSum, so the same values; one
+    // head at a time left each shuffle's latency exposed)
+    float p[G], score[G], bm[G], ps[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float dot = sc[h] + __shfl_xor_sync(0xffffffffu, sc[h], 1);
-      const float score = pos < n ? __fmul_rn(dot, a.scale) : -INFINITY;
-      const float m_new = fmaxf(m[h], WarpMax(score));
-      const float alpha = expf(m[h] - m_new);  // 0 on the first block
-      p[h] = pos < n ? expf(score - m_new) : 0.0f;
-      // each position's p sits on both lanes of its pair: count it once
-      l[h] = fmaf(l[h], alpha, WarpSum(half ? 0.0f : p[h]));
-      m[h] = m_new;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[h][e] *= alpha;
+      score[h] = pos < n ? __fmul_rn(dot, a.scale) : -INFINITY;
+      bm[h] = score[h];
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < G; ++h) bm[h] = fmaxf(bm[h], __shfl_xor_sync(0xffffffffu, bm[h], o));
+    float alpha[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float m_new = fmaxf(m[h], bm[h]);
+      alpha[h] = expf(m[h] - m_new);  // 0 on the first block
+      p[h] = pos < n ? expf(score[h] - m_new) : 0.0f;
+      m[h] = m_new;
+      ps[h] = half ? 0.0f : p[h];  // each position's p sits on both lanes of its pair
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < G; ++h) ps[h] += __shfl_xor_sync(0xffffffffu, ps[h], o);
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      l[h] = fmaf(l[h], alpha[h], ps[h]);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) acc[h][e] *= alpha[h];
+    }
+    // the block's probabilities, G per position, for every lane's P.V
+    if (half == 0 && pos < n) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) sm_p[warp][pos][h] = p[h];
+    }
+    __syncwarp();
     // P.V over the block's positions (V row r: lane owns dims DPL * lane ..)
     for (int r = 0; r < n; ++r) {
       const float* vr = vw + r * HD + DPL * lane;
@@ -334,11 +360,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
         const float2 x = *reinterpret_cast<const float2*>(vr);
         v[0] = x.x; v[1] = x.y;
       }
+      float pr[G];  // position r's probabilities (a shared-memory broadcast)
+      if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int h4 = 0; h4 < G; h4 += 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(&sm_p[warp][r][h4]);
+          pr[h4] = p4.x;
+          pr[h4 + 1] = p4.y;
+          pr[h4 + 2] = p4.z;
+          pr[h4 + 3] = p4.w;
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < G; ++h) pr[h] = sm_p[warp][r][h];
+      }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float pr = __shfl_sync(0xffffffffu, p[h], 2 * r);
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(pr, v[e], acc[h][e]);
+        for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(pr[h], v[e], acc[h][e]);
       }
     }
     __syncwarp();  // every lane is done with this block before it is restaged
