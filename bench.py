@@ -702,20 +702,20 @@ def linear_bench(args):
                 f16 = tc and qt in (wl.Q8_0, wl.Q4_0) and k % 64 == 0
                 line = {
                     "linear": wl.QNAME[qt], "n": n, "k": k, "tokens": t,
-                    "path": ("tcgen05 f16, codes exact, x in 2 pieces" if f16 else
+                    "path": ("tcgen05 f16, d*q and x in 2 exact pieces" if f16 else
                              "tcgen05 tf32x3") if tc else path_name,
                     "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
                     "frac_of_measured": round(gbs / peak, 4),
                     "frac_of_8tbs": round(gbs / SPEC_HBM_GBS, 4),
                     "peak_kind": peak_kind,
                     "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}
-                if f16:  # 2 fp16 products per multiply-add: against the measured bf16 peak
-                    tflops = 2 * 2 * n * k * t / (ms / 1e3) / 1e12
+                if f16:  # 3 fp16 products per multiply-add: against the measured bf16 peak
+                    tflops = 3 * 2 * n * k * t / (ms / 1e3) / 1e12
                     peak_tf = measured_tensor_peak()
                     line.update({"f16_tflops": round(tflops, 1),
                                  "frac_of_tensor_peak": round(tflops / peak_tf, 4)
                                  if peak_tf else None,
-                                 "fp32_equiv_tflops": round(tflops / 2, 1)})
+                                 "fp32_equiv_tflops": round(tflops / 3, 1)})
                 elif tc:  # 3 TF32 products per multiply-add: against the dense TF32 peak
                     tflops = 3 * 2 * n * k * t / (ms / 1e3) / 1e12
                     line.update({"tf32_tflops": round(tflops, 1),

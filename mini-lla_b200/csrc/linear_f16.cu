@@ -1,48 +1,56 @@
-// Prompt-sized Q8_0 / Q4_0 linear layers on the fp16 tensor cores with the
-// weight codes as exact operands: y[t] = W . x[t], W [n, k] in ggml blocks,
-// x [T, k] fp32 — the form mlb_linear_rows_f32 takes for these two formats.
+// Prompt-sized Q8_0 / Q4_0 linear layers on the fp16 tensor cores:
+// y[t] = W . x[t], W [n, k] in ggml blocks, x [T, k] fp32 — the form
+// mlb_linear_rows_f32 takes for these two formats.
 //
 // Reference arithmetic (src/quant.cc:171-226 LinearWithBlocks): per output a
 // sequential fp32 sum of (d * q_i) * x_i, with q_i the int8 code (Q8_0) or
 // n_i - 8 (Q4_0) and d the block's fp16 scale.
 //
-// Method: every code q (|q| <= 128) is exact in fp16.  Each token row of x is
-// scaled by a power of two s_t (its largest magnitude lands in [2^14, 2^15))
-// and split into two fp16 pieces, x / s_t = xh + xl + r, each piece the fp16
-// rounding of the exact fp32 remainder, |r| <= 2^-22 |x / s_t| (plus 2^-25
-// below fp16's normal range, i.e. 2^-39 of the row's largest value).  Per
-// (128-row, 128-token) tile and ggml block the tensor core sums
-// q_i * (xh_i + xl_i) into an fp32 accumulator — every product is exact
-// (8 x 11 significant bits) — with 4 MMAs (tcgen05.mma kind::f16, fp16 A
-// and B, K = 16: two pieces x two halves of the block).  The epilogue adds
-// d * block sum to each output in fp32 registers and finally multiplies by
-// s_t: the block scale never enters the tensor core, so no weight is
-// dequantised or split.  Against the TF32 form (w and x split into head +
-// tail, 3 products of K = 8 per 8 values) this is a third of the tensor-core
-// work per block.  Results stay within the tests' 1e-5 * sum |w_i x_i| of the
-// reference.  A row of x holding Inf or NaN keeps s_t = 1, so the
-// non-finite values reach its outputs.
+// Method: a dequantised weight w = d * q is split into two fp16 pieces
+// without error.  d is an fp16 number, so d and q * d (|q| <= 128) are
+// integer multiples of 2^-24, fp16's smallest step; hi = RN_fp16(q * d) is one
+// too, and the remainder lo = q * d - hi is a multiple of 2^-24 with at most 8
+// significant bits — an fp16 number.  Both come from two packed fp16
+// operations: hi by a rounded multiply, lo by a fused multiply-add of q, d
+// and -hi (exact because its result is representable).  That holds while
+// |q * d| <= 65504, i.e. |d| < 512; a tile that meets a larger or non-finite
+// block scale is recomputed on the CUDA cores (below).  Each token row of x
+// is scaled by a power of two s_t (its largest magnitude lands in
+// [2^14, 2^15)) and split into two fp16 pieces, x / s_t = xh + xl + r,
+// |r| <= 2^-22 |x / s_t| (plus 2^-25 below fp16's normal range, i.e. 2^-39
+// of the row's largest value).  Per (128-row, 128-token) tile the tensor core
+// sums hi.xh + hi.xl + lo.xh over the whole of k into one fp32 accumulator
+// (tcgen05.mma kind::f16, K = 16: 3 MMAs per 16 values; every product is
+// exact, the dropped lo.xl is below 2^-23 of each term), and the epilogue
+// multiplies by s_t.  No per-block rescaling interrupts the accumulation, so
+// the MMAs of consecutive stages queue back to back.  Results stay within
+// the tests' 1e-5 * sum |w_i x_i| of the reference.  A row of x holding Inf
+// or NaN keeps s_t = 1, so the non-finite values reach its outputs.
 //
 // Design (one CTA = 128 weight rows x 128 tokens, k in stages of two blocks;
-// 448 threads in warp roles):
-//   - warp 4, one lane: TMA producer.  Per stage: the raw bytes of the 128
+// 320 threads in warp roles):
+//   - warp 8, one lane: TMA producer.  Per stage: the raw bytes of the 128
 //     rows' two blocks (a 2-D uint8 map over [n, row_bytes], box 128 bytes
 //     from the stage's byte offset rounded down to 16, which covers two 34-
 //     or 18-byte blocks) and the two 128-token x 64-value fp16 tiles of x's
 //     pieces, all with a 128-byte swizzle (bank-conflict-free row reads; the
 //     MMA descriptors use the same layout); 4 stages of 48 KB in flight;
-//   - warps 0-3 (thread = weight row = tensor-memory lane): turn the two
-//     blocks' codes into fp16 pairs (one byte permute builds 1024 + byte in
-//     both halves, one packed subtract — exact) and store them into tensor
-//     memory (tcgen05.st, the A operand; 16 columns per block); the block
-//     scales go to a shared ring;
-//   - warp 5: allocates tensor memory; one lane issues the 4 MMAs of each
-//     block into one of two 128-column fp32 accumulators and commits;
-//   - warps 6-13 (two per tensor-memory lane quarter, 64 tokens each): read
-//     a block's accumulator (tcgen05.ld), add d * sum to 64 fp32 sums per
-//     thread, and at the end store s_t * sum.
+//   - warps 0-7, two threads per weight row (= tensor-memory lane), warps
+//     0-3 the stage's first block and 4-7 its second: turn the block's codes
+//     into fp16 pairs (a byte permute builds 1024 + byte in both halves, one
+//     packed subtract), form hi and lo, and store them into tensor memory
+//     (tcgen05.st, the A operands: 16 columns each per block); at the end
+//     the same warps read the accumulator (tcgen05.ld) and store s_t * sum;
+//   - warp 9: allocates tensor memory; one lane issues the 12 MMAs of each
+//     stage into the accumulator and commits the stage's buffers.
 // Every wait is bounded: a wait that gives up is counted (mlb_wait_timeouts)
 // and the CTA writes NaN instead of its tile.
+//
+// CUDA-core tile (block scales with |d| >= 512, Inf or NaN): the movers flag
+// such a block; the CTA then computes each of its outputs as the GEMV does —
+// per block the fp32 sum of q_i x_i, times d, summed over the blocks — which
+// keeps the reference's Inf / NaN behaviour.  Real model weights have
+// |d| far below 512; the path exists so that no input gives a wrong result.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -61,25 +69,23 @@ constexpr int kHfTokens = 128;      // tokens (MMA N)
 constexpr int kHfStageK = 64;       // values per stage: two ggml blocks
 constexpr int kHfStages = 4;
 constexpr int kHfPieces = 2;        // fp16 pieces of x
-constexpr int kHfThreads = 448;     // movers 0-3, producer 4, MMA 5, epilogue 6-13
+constexpr int kHfMovers = 8;        // warps 0-7: A operands, then the epilogue
+constexpr int kHfThreads = 320;     // movers 0-7, producer 8, MMA 9
 constexpr int kHfRawBytes = kHfRows * 128;               // raw weight box per stage
 constexpr int kHfPieceBytes = kHfTokens * kHfStageK * 2; // one fp16 x piece per stage
 constexpr int kHfStageBytes = kHfRawBytes + kHfPieces * kHfPieceBytes;
-constexpr int kHfScaleSlots = 8;    // stages of block scales kept for the epilogue
 constexpr int kHfTmemColumns = 512;
-constexpr int kHfAccColumns = kHfTokens;  // one fp32 accumulator
-constexpr int kHfAColumns = 32;           // two blocks x 16 columns (2 fp16 each)
+constexpr int kHfAccColumns = kHfTokens;  // the fp32 accumulator
+constexpr int kHfAColumns = 64;           // per stage: hi (2 blocks x 16), then lo
 constexpr int kHfMaxGroup = 3;
 
 __host__ __device__ constexpr int HfBlockBytes(int qt) { return qt == MLB_Q8_0 ? 34 : 18; }
 
 // Shared memory from a 1024-byte aligned base: kHfStages stages (raw box,
-// then x's pieces), the scale ring, the barriers, the TMEM address.
-constexpr int kHfScaleOffset = kHfStages * kHfStageBytes;
-constexpr int kHfBarOffset = kHfScaleOffset + kHfScaleSlots * 2 * kHfRows * 4;
-// raw_full / raw_empty / a_full / a_empty per stage, d_full / d_empty x 2,
-// sc_full / sc_empty per scale slot, mma_done
-constexpr int kHfBarriers = 4 * kHfStages + 4 + 2 * kHfScaleSlots + 1;
+// then x's pieces), the barriers, the TMEM address and two flags.
+constexpr int kHfBarOffset = kHfStages * kHfStageBytes;
+// raw_full / raw_empty / a_full / a_empty per stage, acc_full, mma_done
+constexpr int kHfBarriers = 4 * kHfStages + 2;
 constexpr int kHfSmemBytes = kHfBarOffset + 8 * kHfBarriers + 16 + 1024;
 
 __device__ __forceinline__ uint32_t HfSmem(const void* p) {
@@ -146,17 +152,13 @@ __device__ __forceinline__ void HfCommit(uint32_t bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void HfStore32(uint32_t taddr, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void HfStore16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
-      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
-      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(
-          taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
       "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      "r"(v[15])
       : "memory");
 }
 __device__ __forceinline__ void HfLoad32(uint32_t taddr, float (&v)[32]) {
@@ -189,70 +191,84 @@ __device__ __forceinline__ void HfWordPairs(uint32_t u, uint32_t bias2, uint32_t
 constexpr uint32_t kHfBiasQ8 = 0x64806480u;  // fp16 pair (1152, 1152): 1024 + 128
 constexpr uint32_t kHfBiasQ4 = 0x64086408u;  // fp16 pair (1032, 1032): 1024 + 8
 
-// Row m's two blocks of a raw stage (byte `rel` = 4 R of its 128-byte
-// swizzled box row): 32 A columns (fp16 pairs, K order) and the two fp16
-// scales.
-template <int QT, int R>
-__device__ __forceinline__ void HfTakeStage(const uint8_t* raw_row, int m, uint32_t (&cols)[32],
-                                            uint32_t (&scale)[2]) {
-  constexpr int kChunks = QT == MLB_Q8_0 ? 5 : 3;  // 16-byte pieces covering rel + 2 blocks
-  uint32_t w[4 * kChunks + 1];
+// A code pair q (fp16 x2) and the block scale pair (d, d), -d: the exact
+// pieces hi = RN(q d) and lo = q d - hi (see the top of the file).
+__device__ __forceinline__ void HfSplitPair(uint32_t q, uint32_t d2, uint32_t nd2, uint32_t& hi,
+                                            uint32_t& lo) {
+  uint32_t nh;
+  asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(nh) : "r"(q), "r"(nd2));         // -hi
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(lo) : "r"(q), "r"(d2), "r"(nh));
+  hi = nh ^ 0x80008000u;
+}
+
+// Block J (0 or 1) of a raw stage, row m (its 128-byte swizzled box row; the
+// stage's first block starts at byte 4R): the 16 hi and 16 lo A columns (fp16
+// pairs in K order) and the block scale's bits.
+template <int QT, int R, int J>
+__device__ __forceinline__ void HfTakeBlock(const uint8_t* raw_row, int m, uint32_t (&hi)[16],
+                                            uint32_t (&lo)[16], uint32_t& dbits) {
+  // 16-byte chunks holding the block: Q8_0 bytes [4R + 34J, 4R + 34J + 34),
+  // Q4_0 bytes [4R + 18J, 4R + 18J + 18), R <= 3
+  constexpr int kC0 = QT == MLB_Q8_0 ? 2 * J : J;
+  constexpr int kC1 = QT == MLB_Q8_0 ? 2 * J + 2 : J + 1;
+  uint32_t w[4 * kC1 + 4];
 #pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
+  for (int c = kC0; c <= kC1; ++c) {
     const uint4 v = *reinterpret_cast<const uint4*>(raw_row + 16 * (c ^ (m & 7)));
     w[4 * c] = v.x;
     w[4 * c + 1] = v.y;
     w[4 * c + 2] = v.z;
     w[4 * c + 3] = v.w;
   }
-  w[4 * kChunks] = 0;
+  uint32_t q[16];
   if constexpr (QT == MLB_Q8_0) {
-    // block 0 at byte 4R: scale in the low half of word R, codes from byte
-    // 4R + 2 (a half-word shift); block 1 at 4R + 34: scale in the high half
-    // of word R + 8, codes word-aligned from word R + 9
-    scale[0] = w[R] & 0xFFFFu;
-    scale[1] = w[R + 8] >> 16;
+    // block 0: scale in the low half of word R, codes from byte 4R + 2 (a
+    // half-word shift); block 1 (byte 4R + 34): scale in the high half of
+    // word R + 8, codes word-aligned from word R + 9
+    dbits = J == 0 ? (w[R] & 0xFFFFu) : (w[R + 8] >> 16);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t c0 = __funnelshift_r(w[R + i], w[R + i + 1], 16) ^ 0x80808080u;
-      const uint32_t c1 = w[R + 9 + i] ^ 0x80808080u;
-      HfWordPairs(c0, kHfBiasQ8, cols[2 * i], cols[2 * i + 1]);
-      HfWordPairs(c1, kHfBiasQ8, cols[16 + 2 * i], cols[16 + 2 * i + 1]);
+      const uint32_t c = J == 0 ? __funnelshift_r(w[R + i], w[R + i + 1], 16) : w[R + 9 + i];
+      HfWordPairs(c ^ 0x80808080u, kHfBiasQ8, q[2 * i], q[2 * i + 1]);
     }
   } else {
-    // Q4_0 18-byte blocks: block 0 at 4R (nibbles from 4R + 2), block 1 at
-    // 4R + 18 (scale in the high half of word R + 4, nibbles word-aligned
-    // from word R + 5); values 0-15 are the low nibbles, 16-31 the high ones
-    scale[0] = w[R] & 0xFFFFu;
-    scale[1] = w[R + 4] >> 16;
+    // Q4_0: block 0 nibbles from byte 4R + 2, block 1 (byte 4R + 18): scale
+    // in the high half of word R + 4, nibbles word-aligned from word R + 5;
+    // values 0-15 are the low nibbles, 16-31 the high ones
+    dbits = J == 0 ? (w[R] & 0xFFFFu) : (w[R + 4] >> 16);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t u0 = __funnelshift_r(w[R + i], w[R + i + 1], 16);
-      const uint32_t u1 = w[R + 5 + i];
-      HfWordPairs(u0 & 0x0F0F0F0Fu, kHfBiasQ4, cols[2 * i], cols[2 * i + 1]);
-      HfWordPairs((u0 >> 4) & 0x0F0F0F0Fu, kHfBiasQ4, cols[8 + 2 * i], cols[8 + 2 * i + 1]);
-      HfWordPairs(u1 & 0x0F0F0F0Fu, kHfBiasQ4, cols[16 + 2 * i], cols[16 + 2 * i + 1]);
-      HfWordPairs((u1 >> 4) & 0x0F0F0F0Fu, kHfBiasQ4, cols[24 + 2 * i], cols[24 + 2 * i + 1]);
+      const uint32_t u = J == 0 ? __funnelshift_r(w[R + i], w[R + i + 1], 16) : w[R + 5 + i];
+      HfWordPairs(u & 0x0F0F0F0Fu, kHfBiasQ4, q[2 * i], q[2 * i + 1]);
+      HfWordPairs((u >> 4) & 0x0F0F0F0Fu, kHfBiasQ4, q[8 + 2 * i], q[8 + 2 * i + 1]);
     }
   }
+  const uint32_t d2 = dbits | (dbits << 16);
+  const uint32_t nd2 = d2 ^ 0x80008000u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) HfSplitPair(q[i], d2, nd2, hi[i], lo[i]);
 }
 
-template <int QT>
-__device__ __forceinline__ void HfTakeStageAt(int r, const uint8_t* raw_row, int m,
-                                              uint32_t (&cols)[32], uint32_t (&scale)[2]) {
+template <int QT, int J>
+__device__ __forceinline__ void HfTakeBlockAt(int r, const uint8_t* raw_row, int m,
+                                              uint32_t (&hi)[16], uint32_t (&lo)[16],
+                                              uint32_t& dbits) {
   switch (r) {
-    case 0: HfTakeStage<QT, 0>(raw_row, m, cols, scale); break;
-    case 1: HfTakeStage<QT, 1>(raw_row, m, cols, scale); break;
-    case 2: HfTakeStage<QT, 2>(raw_row, m, cols, scale); break;
-    default: HfTakeStage<QT, 3>(raw_row, m, cols, scale); break;
+    case 0: HfTakeBlock<QT, 0, J>(raw_row, m, hi, lo, dbits); break;
+    case 1: HfTakeBlock<QT, 1, J>(raw_row, m, hi, lo, dbits); break;
+    case 2: HfTakeBlock<QT, 2, J>(raw_row, m, hi, lo, dbits); break;
+    default: HfTakeBlock<QT, 3, J>(raw_row, m, hi, lo, dbits); break;
   }
 }
 
 struct HfGroup {
   CUtensorMap w[kHfMaxGroup];  // raw weight bytes of each matrix
   CUtensorMap x[kHfPieces];    // x's fp16 pieces [T, k]
+  const uint8_t* wp[kHfMaxGroup];  // the same weights, for the CUDA-core tile
   float* y[kHfMaxGroup];
+  const float* x32;            // x [T, k] fp32, for the CUDA-core tile
   const float* row_scale;      // s_t per token
+  int64_t row_bytes;
   int n[kHfMaxGroup];
   int tile_begin[kHfMaxGroup + 1];  // first tile of each matrix; [count] = total
   int count;
@@ -260,6 +276,47 @@ struct HfGroup {
   int t_rows;
   int k;
 };
+
+// The tile's outputs on the CUDA cores: per output and block the fp32 sum
+// of q_i x_i, times d, summed over the blocks (lanes take blocks, then a
+// warp reduction).
+template <int QT>
+__device__ void HfCudaCoreTile(const HfGroup& grp, int mat, int n0, int t0) {
+  constexpr int kBB = HfBlockBytes(QT);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nb = grp.k / 32;
+  const int n = grp.n[mat];
+  for (int r = warp; r < kHfRows && n0 + r < n; r += kHfThreads / 32) {
+    const uint8_t* wrow = grp.wp[mat] + static_cast<int64_t>(n0 + r) * grp.row_bytes;
+    for (int t = t0; t < t0 + kHfTokens && t < grp.t_rows; ++t) {
+      const float* xr = grp.x32 + static_cast<int64_t>(t) * grp.k;
+      float acc = 0.0f;
+      for (int b = lane; b < nb; b += 32) {
+        const uint8_t* blk = wrow + b * kBB;
+        const float d = __half2float(*reinterpret_cast<const __half*>(blk));
+        const float* xb = xr + 32 * b;
+        float sum = 0.0f;
+        if constexpr (QT == MLB_Q8_0) {
+#pragma unroll 8
+          for (int i = 0; i < 32; ++i)
+            sum = fmaf(static_cast<float>(static_cast<int8_t>(blk[2 + i])), xb[i], sum);
+        } else {
+#pragma unroll 8
+          for (int i = 0; i < 16; ++i)
+            sum = fmaf(static_cast<float>((blk[2 + i] & 15) - 8), xb[i], sum);
+#pragma unroll 8
+          for (int i = 0; i < 16; ++i)
+            sum = fmaf(static_cast<float>((blk[2 + i] >> 4) - 8), xb[16 + i], sum);
+        }
+        acc = fmaf(d, sum, acc);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) grp.y[mat][static_cast<int64_t>(t) * n + n0 + r] = acc;
+    }
+  }
+}
 
 }  // namespace
 
@@ -277,19 +334,16 @@ __global__ void __launch_bounds__(kHfThreads, 1)
   uint8_t* base = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sbase = HfSmem(base);
   auto stage_base = [&](int s) { return base + s * kHfStageBytes; };
-  float* scales = reinterpret_cast<float*>(base + kHfScaleOffset);
   const uint32_t bars = sbase + kHfBarOffset;
   auto raw_full = [&](int s) { return bars + 8 * s; };
   auto raw_empty = [&](int s) { return bars + 8 * (kHfStages + s); };
   auto a_full = [&](int s) { return bars + 8 * (2 * kHfStages + s); };
   auto a_empty = [&](int s) { return bars + 8 * (3 * kHfStages + s); };
-  auto d_full = [&](int s) { return bars + 8 * (4 * kHfStages + s); };
-  auto d_empty = [&](int s) { return bars + 8 * (4 * kHfStages + 2 + s); };
-  auto sc_full = [&](int s) { return bars + 8 * (4 * kHfStages + 4 + s); };
-  auto sc_empty = [&](int s) { return bars + 8 * (4 * kHfStages + 4 + kHfScaleSlots + s); };
-  const uint32_t mma_done = bars + 8 * (4 * kHfStages + 4 + 2 * kHfScaleSlots);
+  const uint32_t acc_full = bars + 8 * (4 * kHfStages);
+  const uint32_t mma_done = bars + 8 * (4 * kHfStages + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kHfBarOffset + 8 * kHfBarriers);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* cuda_core_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -304,23 +358,17 @@ __global__ void __launch_bounds__(kHfThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kHfStages; ++s) {
       HfBarInit(raw_full(s), 1);
-      HfBarInit(raw_empty(s), 5);  // the 4 mover warps + the MMA commit
-      HfBarInit(a_full(s), 4);
+      HfBarInit(raw_empty(s), kHfMovers + 1);  // the mover warps + the MMA commit
+      HfBarInit(a_full(s), kHfMovers);
       HfBarInit(a_empty(s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      HfBarInit(d_full(s), 1);
-      HfBarInit(d_empty(s), 8);
-    }
-    for (int s = 0; s < kHfScaleSlots; ++s) {
-      HfBarInit(sc_full(s), 4);
-      HfBarInit(sc_empty(s), 8);
-    }
+    HfBarInit(acc_full, 1);
     HfBarInit(mma_done, 1);
     *abort_flag = 0;
+    *cuda_core_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      HfSmem(tmem_slot)),
                  "r"(kHfTmemColumns)
@@ -331,12 +379,11 @@ __global__ void __launch_bounds__(kHfThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
   const uint32_t tmem = *tmem_slot;
-  // tensor-memory columns: two accumulators, then the A ring
-  auto acc_col = [&](int b) { return static_cast<uint32_t>(b * kHfAccColumns); };
-  auto a_col = [&](int s) { return static_cast<uint32_t>(2 * kHfAccColumns + s * kHfAColumns); };
+  // tensor-memory columns: the accumulator, then the A ring
+  auto a_col = [&](int s) { return static_cast<uint32_t>(kHfAccColumns + s * kHfAColumns); };
 
   int issued = 0;  // producer: stages whose loads were issued
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       for (int s = 0; s < stages; ++s) {
         const int st = s % kHfStages;
@@ -355,119 +402,103 @@ __global__ void __launch_bounds__(kHfThreads, 1)
         issued = s + 1;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       bool ok = true;
-      for (int s = 0; ok && s < stages; ++s) {
+      for (int s = 0; s < stages; ++s) {
         const int st = s % kHfStages;
         if (!HfWait(raw_full(st), (s / kHfStages) & 1) ||
             !HfWait(a_full(st), (s / kHfStages) & 1) || *abort_flag) {
           ok = false;
           break;
         }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
         const uint32_t pieces = HfSmem(stage_base(st) + kHfRawBytes);
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {  // the stage's two blocks
-          const int b = 2 * s + j;
-          if (!HfWait(d_empty(b & 1), ((b >> 1) & 1) ^ 1) || *abort_flag) {
-            ok = false;
-            break;
+        for (int j = 0; j < 2; ++j)      // the stage's two blocks
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // K = 16 per MMA: 32 bytes of the 128-byte rows
+            const uint32_t a_hi = tmem + a_col(st) + 16 * j + 8 * h;
+            const uint64_t bh = HfDesc(pieces + 64 * j + 32 * h);
+            const uint64_t bl = HfDesc(pieces + kHfPieceBytes + 64 * j + 32 * h);
+            HfMma(tmem, a_hi, bh, (s | j | h) != 0);
+            HfMma(tmem, a_hi, bl, 1);
+            HfMma(tmem, a_hi + 32, bh, 1);
           }
-          asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-#pragma unroll
-          for (int p = 0; p < kHfPieces; ++p)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)  // K = 16 per MMA: 32 bytes of the 128-byte rows
-              HfMma(tmem + acc_col(b & 1), tmem + a_col(st) + 16 * j + 8 * h,
-                    HfDesc(pieces + p * kHfPieceBytes + 64 * j + 32 * h), (p | h) != 0);
-          HfCommit(d_full(b & 1));
-        }
-        if (!ok) break;
         HfCommit(a_empty(st));
         HfCommit(raw_empty(st));
       }
-      if (!ok) {
+      if (ok) {
+        HfCommit(acc_full);
+      } else {
         atomicAdd(&g_hf_wait_timeouts, 1u);
         *abort_flag = 1;
       }
     }
-  } else if (warp < 4) {
-    // ---- movers: codes -> fp16 pairs in tensor memory, scales -> shared ----
-    const int m = threadIdx.x;  // weight row within the tile (TMEM lane)
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  } else {
+    // ---- movers: block j of each stage -> hi / lo pairs in tensor memory ----
+    const int j = warp >> 2;                  // the stage's block
+    const int m = (warp & 3) * 32 + lane;     // weight row within the tile (TMEM lane)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    uint32_t big = 0;
     for (int s = 0; s < stages; ++s) {
       const int st = s % kHfStages;
-      const int ss = s % kHfScaleSlots;
-      if (!HfWait(raw_full(st), (s / kHfStages) & 1) ||
-          !HfWait(a_empty(st), ((s / kHfStages) & 1) ^ 1) ||
-          !HfWait(sc_empty(ss), ((s / kHfScaleSlots) & 1) ^ 1) || *abort_flag) {
-        atomicAdd(&g_hf_wait_timeouts, 1u);
+      // one decision per warp: the tensor-memory stores below need all lanes
+      const bool ready = HfWait(raw_full(st), (s / kHfStages) & 1) &&
+                         HfWait(a_empty(st), ((s / kHfStages) & 1) ^ 1) && !*abort_flag;
+      if (!__all_sync(0xffffffffu, ready)) {
+        if (lane == 0) atomicAdd(&g_hf_wait_timeouts, 1u);
         *abort_flag = 1;
         break;
       }
-      uint32_t cols[32], sc[2];
-      HfTakeStageAt<QT>(((s * 2 * kBB) & 15) >> 2, stage_base(st) + m * 128, m, cols, sc);
+      uint32_t hi[16], lo[16], dbits;
+      const int r = ((s * 2 * kBB) & 15) >> 2;
+      if (j == 0)
+        HfTakeBlockAt<QT, 0>(r, stage_base(st) + m * 128, m, hi, lo, dbits);
+      else
+        HfTakeBlockAt<QT, 1>(r, stage_base(st) + m * 128, m, hi, lo, dbits);
+      big |= (dbits & 0x7FFFu) >= 0x6000u;  // |d| >= 512, Inf or NaN
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-      HfStore32(lane_base + a_col(st), cols);
-      float* sl = scales + ss * 2 * kHfRows;
-      sl[m] = __half2float(__ushort_as_half(static_cast<unsigned short>(sc[0])));
-      sl[kHfRows + m] = __half2float(__ushort_as_half(static_cast<unsigned short>(sc[1])));
+      HfStore16(lane_base + a_col(st) + 16 * j, hi);
+      HfStore16(lane_base + a_col(st) + 32 + 16 * j, lo);
       asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
       __syncwarp();
       if (lane == 0) {
         HfArrive(a_full(st));
-        HfArrive(sc_full(ss));
         HfArrive(raw_empty(st));  // this warp is done with the raw box
       }
     }
-  } else {
-    // ---- epilogue: block sums * d -> 64 fp32 sums per thread ----
-    const int q = warp & 3;            // tensor-memory lane quarter
-    const int half = (warp - 6) >> 2;  // tokens [64 half, 64 half + 64)
-    const int m = q * 32 + lane;       // weight row
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
-    bool ok = true;
-    for (int b = 0; b < 2 * stages; ++b) {
-      const int ss = (b >> 1) % kHfScaleSlots;
-      if (((b & 1) == 0 && !HfWait(sc_full(ss), ((b >> 1) / kHfScaleSlots) & 1)) ||
-          !HfWait(d_full(b & 1), (b >> 1) & 1) || *abort_flag) {
-        ok = false;
-        break;
-      }
+    if (__any_sync(0xffffffffu, big) && lane == 0) *cuda_core_flag = 1;
+  }
+
+  __syncthreads();
+  const bool cuda_core = *cuda_core_flag != 0;
+  if (warp < kHfMovers && !*abort_flag && !cuda_core) {
+    // ---- epilogue: warps w and w + 4 share lanes 32 (w & 3).., 64 tokens each ----
+    if (!__all_sync(0xffffffffu, HfWait(acc_full, 0))) {
+      if (lane == 0) atomicAdd(&g_hf_wait_timeouts, 1u);
+      *abort_flag = 1;
+    } else {
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-      const float d = scales[ss * 2 * kHfRows + (b & 1) * kHfRows + m];
+      const int q = warp & 3;
+      const int half = warp >> 2;
+      const int row = n0 + q * 32 + lane;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      float* y = grp.y[mat];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {  // 32 tokens at a time
         float v[32];
-        HfLoad32(lane_base + acc_col(b & 1) + 64 * half + 32 * c, v);
+        HfLoad32(lane_base + 64 * half + 32 * c, v);
         asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+        if (row < n) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[32 * c + i] = fmaf(d, v[i], acc[32 * c + i]);
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        HfArrive(d_empty(b & 1));
-        if (b & 1) HfArrive(sc_empty(ss));  // both blocks of the stage read
-      }
-    }
-    if (!ok) {
-      if (lane == 0) atomicAdd(&g_hf_wait_timeouts, 1u);
-      *abort_flag = 1;
-    }
-    const int row = n0 + m;
-    if (row < n) {
-      float* y = grp.y[mat];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int t = t0 + 64 * half + i;
-        if (t < grp.t_rows)
-          y[static_cast<int64_t>(t) * n + row] =
-              ok ? acc[i] * __ldg(grp.row_scale + t) : __int_as_float(0x7fc00000);
+          for (int i = 0; i < 32; ++i) {
+            const int t = t0 + 64 * half + 32 * c + i;
+            if (t < grp.t_rows)
+              y[static_cast<int64_t>(t) * n + row] = v[i] * __ldg(grp.row_scale + t);
+          }
+        }
       }
     }
   }
@@ -475,7 +506,7 @@ __global__ void __launch_bounds__(kHfThreads, 1)
   __syncthreads();
   if (*abort_flag) {
     // let the loads in flight land and mark the whole tile as failed
-    if (warp == 4 && lane == 0) {
+    if (warp == 8 && lane == 0) {
       for (int s = issued - kHfStages > 0 ? issued - kHfStages : 0; s < issued; ++s)
         HfWait(raw_full(s % kHfStages), (s / kHfStages) & 1);
     }
@@ -485,15 +516,17 @@ __global__ void __launch_bounds__(kHfThreads, 1)
         for (int t = t0; t < t0 + kHfTokens && t < grp.t_rows; ++t)
           grp.y[mat][static_cast<int64_t>(t) * n + row] = __int_as_float(0x7fc00000);
     }
+  } else if (cuda_core) {
+    HfCudaCoreTile<QT>(grp, mat, n0, t0);
   }
-  if (warp == 5 && lane == 0) {
+  if (warp == 9 && lane == 0) {
     // every MMA issued has finished before the tensor memory is released
     HfCommit(mma_done);
     HfWait(mma_done, 0);
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
                  "r"(kHfTmemColumns)
@@ -613,6 +646,7 @@ int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int6
     if (!HfMap2D(&grp.w[m], CU_TENSOR_MAP_DATA_TYPE_UINT8, w[m], static_cast<uint64_t>(row_bytes),
                  static_cast<uint64_t>(n[m]), static_cast<uint64_t>(row_bytes), 128, kHfRows))
       return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: tensor map encoding failed");
+    grp.wp[m] = static_cast<const uint8_t*>(w[m]);
     grp.y[m] = y[m];
     grp.n[m] = static_cast<int>(n[m]);
     grp.tile_begin[m] = static_cast<int>(tiles);
@@ -636,6 +670,8 @@ int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int6
                kHfTokens))
     return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: tensor map encoding failed");
   grp.row_scale = row_scale;
+  grp.x32 = x;
+  grp.row_bytes = row_bytes;
   auto kernel = qtype == MLB_Q8_0 ? LinearF16Kernel<MLB_Q8_0> : LinearF16Kernel<MLB_Q4_0>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHfSmemBytes) !=
       cudaSuccess) {

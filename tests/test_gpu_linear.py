@@ -122,6 +122,60 @@ def test_linear_rows_large_values_and_small_batches(cuda, oracle):
         _check(got.cpu().numpy(), want, wdeq, x, f"rows wide-range t={t}")
 
 
+def _set_scale(table, qtype, k, row, block, d):
+    bb = wl.BLOCK_BYTES[qtype]
+    at = (row * (k // 32) + block) * bb
+    table[at:at + 2] = np.array([d], dtype=np.float16).view(np.uint8)
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0])
+def test_linear_rows_block_scale_edges(cuda, oracle, qtype):
+    """Block scales at the edges of the fp16 split of d * q: the largest
+    that keeps it exact (511.75, with code -128 for Q8_0), subnormal ones
+    (2^-24, 1e-6), decades apart inside one row, negative; and one of 1000,
+    which sends its 128 x 128 tile to the CUDA cores.  Every output within
+    the bar, ragged tiles in n and t."""
+    import torch
+    n, k, t = 300, 1024, 130
+    rng = np.random.default_rng(qtype + 11)
+    table = wl.numpy_quant_table(qtype, n, k, seed=21)
+    _set_scale(table, qtype, k, 5, 3, 511.75)
+    if qtype == wl.Q8_0:
+        at = (5 * (k // 32) + 3) * 34 + 2
+        table[at] = 0x80  # code -128
+    for b, d in enumerate([2.0 ** -24, 1e-6, 6e-5, 1e-3, 10.0, 300.0, -0.02, -2.0 ** -20] * 4):
+        _set_scale(table, qtype, k, 7, b, d)
+    _set_scale(table, qtype, k, 200, 10, 1000.0)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear_rows(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"scale edges {wl.QNAME[qtype]}")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0])
+def test_linear_rows_non_finite_block_scale(cuda, oracle, qtype):
+    """An Inf or NaN block scale makes that row's outputs non-finite, as in
+    the reference's sum; the other rows of its tile (computed on the CUDA
+    cores) and of the other tiles stay within the bar."""
+    import torch
+    n, k, t = 256, 512, 64
+    rng = np.random.default_rng(qtype + 12)
+    table = wl.numpy_quant_table(qtype, n, k, seed=22)
+    _set_scale(table, qtype, k, 40, 4, np.inf)
+    _set_scale(table, qtype, k, 170, 0, np.nan)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear_rows(dev(table, cuda), qtype, n, k, dev(x, cuda)).cpu().numpy()
+    assert mlb.wait_timeouts() == 0
+    assert not np.isfinite(got[:, 40]).any() and not np.isfinite(got[:, 170]).any()
+    keep = np.array([r for r in range(n) if r not in (40, 170)])
+    wdeq, _ = oracle.embedding(table, qtype, n, k, keep.astype(np.int32))
+    _check(got[:, keep], want[:, keep], wdeq, x, f"non-finite scale {wl.QNAME[qtype]}")
+
+
 @pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_1, wl.F32])
 @pytest.mark.parametrize("t", [5, 64, 200])
 def test_linear_rows_group_vs_single(cuda, oracle, qtype, t):
