@@ -404,6 +404,9 @@ __global__ void __launch_bounds__(kHfThreads, 1)
     }
   } else if (warp == 9) {
     if (lane == 0) {
+      // shared-memory descriptors are built once: an offset below 256 KB adds
+      // to the descriptor's 14-bit address field (in 16-byte units)
+      const uint64_t desc0 = HfDesc(HfSmem(stage_base(0) + kHfRawBytes));
       bool ok = true;
       for (int s = 0; s < stages; ++s) {
         const int st = s % kHfStages;
@@ -413,14 +416,15 @@ __global__ void __launch_bounds__(kHfThreads, 1)
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const uint32_t pieces = HfSmem(stage_base(st) + kHfRawBytes);
+        const uint64_t desc = desc0 + static_cast<uint64_t>(st * (kHfStageBytes >> 4));
+        const uint32_t a_st = tmem + a_col(st);
 #pragma unroll
         for (int j = 0; j < 2; ++j)      // the stage's two blocks
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // K = 16 per MMA: 32 bytes of the 128-byte rows
-            const uint32_t a_hi = tmem + a_col(st) + 16 * j + 8 * h;
-            const uint64_t bh = HfDesc(pieces + 64 * j + 32 * h);
-            const uint64_t bl = HfDesc(pieces + kHfPieceBytes + 64 * j + 32 * h);
+            const uint32_t a_hi = a_st + 16 * j + 8 * h;
+            const uint64_t bh = desc + ((64 * j + 32 * h) >> 4);
+            const uint64_t bl = desc + ((kHfPieceBytes + 64 * j + 32 * h) >> 4);
             HfMma(tmem, a_hi, bh, (s | j | h) != 0);
             HfMma(tmem, a_hi, bl, 1);
             HfMma(tmem, a_hi + 32, bh, 1);

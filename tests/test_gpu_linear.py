@@ -91,9 +91,10 @@ def test_linear_rejects_bad_input(cuda):
 @pytest.mark.parametrize("n,k,t", [(128, 256, 48), (300, 4096, 49), (64, 1024, 128),
                                    (200, 512, 200), (129, 3584, 64), (1000, 4096, 257)])
 def test_linear_rows_tensor_cores_vs_oracle(cuda, oracle, qtype, n, k, t):
-    """Prompt-sized batches (>= 48 tokens) run on the tcgen05 TF32 path with
-    head + tail splits; same 1e-5 * sum|w x| bar as the GEMV, every output
-    (ragged tiles in both n and t included)."""
+    """Prompt-sized batches (>= 48 tokens) run on the tensor cores: Q8_0 /
+    Q4_0 with d * q and x in exact fp16 pieces, Q4_1 / F32 with TF32 head +
+    tail splits; same 1e-5 * sum|w x| bar as the GEMV, every output (ragged
+    tiles in both n and t included)."""
     import torch
     rng = np.random.default_rng(n + 3 * k + 7 * t)
     table = wl.numpy_quant_table(qtype, n, k, seed=n + k + t)
@@ -153,6 +154,48 @@ def test_linear_rows_block_scale_edges(cuda, oracle, qtype):
     assert mlb.wait_timeouts() == 0
     wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
     _check(got.cpu().numpy(), want, wdeq, x, f"scale edges {wl.QNAME[qtype]}")
+
+
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0])
+def test_linear_rows_many_tiles(cuda, oracle, qtype):
+    """More 128 x 128 tiles than SMs (30 row tiles x 5 token tiles, a second
+    wave of CTAs): within the bar, and two calls agree bit for bit."""
+    import torch
+    n, k, t = 3840, 512, 640
+    rng = np.random.default_rng(qtype + 13)
+    table = wl.numpy_quant_table(qtype, n, k, seed=23)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    w, xd = dev(table, cuda), dev(x, cuda)
+    a = mlb.linear_rows(w, qtype, n, k, xd)
+    b = mlb.linear_rows(w, qtype, n, k, xd)
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    assert torch.equal(a, b)
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(a.cpu().numpy(), want, wdeq, x, f"many tiles {wl.QNAME[qtype]}")
+
+
+def test_linear_rows_many_tiles_cuda_core(cuda, oracle):
+    """Block scales of 1000 in the first stage of even row tiles and the last
+    stage of odd ones: those tiles go to the CUDA cores, beside tensor-core
+    tiles in the same launch."""
+    import torch
+    n, k, t = 3840, 512, 640
+    rng = np.random.default_rng(14)
+    table = wl.numpy_quant_table(wl.Q8_0, n, k, seed=24)
+    for rt in range(n // 128):
+        if rt % 2 == 0:
+            _set_scale(table, wl.Q8_0, k, 128 * rt + 3, 1, 1000.0)
+        else:
+            _set_scale(table, wl.Q8_0, k, 128 * rt + 7, k // 32 - 1, -1000.0)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    want = oracle.linear(table, wl.Q8_0, n, k, x)
+    got = mlb.linear_rows(dev(table, cuda), wl.Q8_0, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    wdeq, _ = oracle.embedding(table, wl.Q8_0, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, "many tiles, CUDA-core tiles")
 
 
 @pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0])
