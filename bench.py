@@ -633,6 +633,7 @@ def gpu_arm(args, cfg):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
         "timing": "cuda graph replay" if use_graph else "direct launches",
+        "launch_overlap": args.launch_overlap,
         "gpu_launches": args.steps * len(step.ops),
     }
     if cpu is not None:
@@ -781,7 +782,8 @@ def prefill_bench(args):
     cmd = [PREFILL_EXE, "--layers", str(args.prefill_layers), "--tokens",
            str(args.prefill_tokens), "--type", args.prefill_type,
            "--steps", str(max(1, min(args.steps, 10))), "--warmup", str(max(1, args.warmup)),
-           "--max-rows", str(max(512, args.prefill_tokens))]
+           "--max-rows", str(max(512, args.prefill_tokens)),
+           "--overlap", str(args.launch_overlap)]
     if args.no_cpu_baseline:
         cmd += ["--cpu-tokens", "0"]
     res = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
@@ -967,11 +969,17 @@ def main():
     ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1, 2),
                     help="decode linear kernel: 0 automatic, 1 CUDA-core GEMV, "
                          "2 int8 tensor-core GEMV where allowed")
+    ap.add_argument("--launch-overlap", type=int, default=1, choices=(0, 1),
+                    help="1: programmatic dependent launch between kernels (the "
+                         "library's default), 0: plain stream order")
     ap.add_argument("--sweep-ops", default="")
     ap.add_argument("--sweep-hidden", default="")
     ap.add_argument("--sweep-tokens", default="")
     args = ap.parse_args()
     cfg = wl.CONFIGS[args.workload]
+    if args.impl != "reference" and not args.prefill:
+        import mlb
+        mlb.set_launch_overlap(args.launch_overlap)
     if args.sweep:
         sweep(args)
         return

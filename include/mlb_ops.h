@@ -219,6 +219,19 @@ int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
 int mlb_set_gemv_path(int path);
 int mlb_gemv_path(void);
 
+/*
+ * Launch overlap: 1 (the default) launches every kernel with programmatic
+ * dependent launch, so that a kernel's launch and set-up overlap the tail of
+ * the stream's previous kernel (each kernel first waits, on the device, for
+ * the previous one to complete and its writes to be visible); 0 launches them
+ * one after another.  Results are the same either way.  Process-wide; for
+ * benchmarks and tests.  Returns MLB_OK, or MLB_ERR_ARG for another value;
+ * mlb_launch_overlap returns the current setting.  No counterpart in the
+ * reference.
+ */
+int mlb_set_launch_overlap(int on);
+int mlb_launch_overlap(void);
+
 /* Floats of scratch mlb_linear_rows_f32 needs for t_rows tokens of k values
  * (-1 for bad arguments). */
 int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows);

@@ -65,6 +65,8 @@ int Splits(int n_kv_heads, int64_t visible, int64_t rows = 1) {
 
 template <int G, int NV>
 __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float sm_m[kAttnWarps][G];
   __shared__ float sm_l[kAttnWarps][G];
   __shared__ float4 sm_acc[kAttnWarps][G][32 * NV];
@@ -189,6 +191,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
 
 // out[h][i] = sum_s acc_s[i] * e^(m_s - M) / sum_s l_s * e^(m_s - M).
 __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int head = blockIdx.x;
   const int64_t row = blockIdx.y;
   const float* base = a.scratch + (row * a.n_heads + head) * a.splits * (a.hd + 2);
@@ -234,6 +238,8 @@ __host__ __device__ constexpr int LaneWarpFloats() {  // K block + V block
 
 template <int G, int HD4>
 __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   constexpr int HD = 4 * HD4;
   constexpr int DPL = HD / 32;        // dimensions per lane in P.V (2 or 4)
   constexpr int KRF = LaneKRowFloats<HD4>();
@@ -431,7 +437,7 @@ int LaunchLane(const AttnArgs& a, dim3 grid, cudaStream_t s) {
     cudaGetLastError();
     return Fail(MLB_ERR_CUDA, "attention: shared memory opt-in");
   }
-  kernel<<<grid, kAttnWarps * 32, shm, s>>>(a);
+  Launch(kernel, grid, kAttnWarps * 32, shm, s, a);
   return CheckLaunch("mlb_attention_decode_f32");
 }
 
@@ -444,9 +450,9 @@ int LaunchPartial(const AttnArgs& a, int64_t rows, int nv, cudaStream_t s) {
   } else if (a.hd == 64) {
     return LaunchLane<G, 16>(a, grid, s);
   } else if (nv == 1) {
-    AttnPartialKernel<G, 1><<<grid, kAttnWarps * 32, 0, s>>>(a);
+    Launch(AttnPartialKernel<G, 1>, grid, kAttnWarps * 32, 0, s, a);
   } else {
-    AttnPartialKernel<G, 2><<<grid, kAttnWarps * 32, 0, s>>>(a);
+    Launch(AttnPartialKernel<G, 2>, grid, kAttnWarps * 32, 0, s, a);
   }
   return CheckLaunch("mlb_attention_decode_f32");
 }
@@ -454,6 +460,8 @@ int LaunchPartial(const AttnArgs& a, int64_t rows, int nv, cudaStream_t s) {
 __global__ void __launch_bounds__(256)
     KvWriteKernel(float* keys, float* values, const float* k, const float* v,
                   int64_t base, int64_t count) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        i < count; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     keys[base + i] = k[i];
@@ -528,6 +536,8 @@ constexpr size_t TileSmemBytes() {
 
 template <int G, int HD4>
 __global__ void __launch_bounds__(kTileThreads, 1) AttnRowTileKernel(AttnTileArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   constexpr int QR = kTileQv / G;  // query rows per CTA
   constexpr int QV = QR * G;
   constexpr int RF = TileRowFloats<HD4>();
@@ -716,7 +726,7 @@ int LaunchRowTile(const AttnTileArgs& a, cudaStream_t s) {
   }
   const dim3 grid(static_cast<unsigned>(a.n_kv_heads),
                   static_cast<unsigned>((a.rows + QR - 1) / QR));
-  kernel<<<grid, kTileThreads, shm, s>>>(a);
+  Launch(kernel, grid, kTileThreads, shm, s, a);
   return CheckLaunch("attention (row tiles)");
 }
 
@@ -804,8 +814,7 @@ int AttentionRows(const float* q, const float* keys, const float* values, float*
       case 8: rc = LaunchPartial<8>(a, rc_rows, nv, s); break;
     }
     if (rc != MLB_OK) return rc;
-    AttnCombineKernel<<<dim3(n_heads, static_cast<unsigned>(rc_rows)),
-                        hd < 256 ? ((hd + 31) / 32) * 32 : 256, 0, s>>>(a);
+    Launch(AttnCombineKernel, dim3(n_heads, static_cast<unsigned>(rc_rows)), hd < 256 ? ((hd + 31) / 32) * 32 : 256, 0, s, a);
     rc = CheckLaunch("attention");
     if (rc != MLB_OK) return rc;
   }
@@ -882,8 +891,7 @@ extern "C" int mlb_kv_write_f32(float* keys, float* values, const float* k,
   const int64_t per = static_cast<int64_t>(n_kv_heads) * head_dim;
   const int64_t count = rows * per;
   const int64_t blocks = (count + 255) / 256;
-  KvWriteKernel<<<static_cast<unsigned>(blocks < 65535 * 16 ? blocks : 65535 * 16),
-                  256, 0, AsStream(stream)>>>(keys, values, k, v, position * per,
+  Launch(KvWriteKernel, static_cast<unsigned>(blocks < 65535 * 16 ? blocks : 65535 * 16), 256, 0, AsStream(stream), keys, values, k, v, position * per,
                                               count);
   return CheckLaunch("mlb_kv_write_f32");
 }

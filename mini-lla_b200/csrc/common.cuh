@@ -26,11 +26,45 @@ inline bool Aligned16(const void* p) {
 
 inline cudaStream_t AsStream(void* s) { return static_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch (on unless mlb_set_launch_overlap(0)): a
+// kernel launched through Launch may start while the stream's previous kernel
+// is still running, so that its launch and set-up overlap that kernel's
+// tail.  Every kernel of this library begins with LaunchWait(), which returns
+// once the previous kernel has completed and its writes are visible, before
+// it reads or writes global memory; it then calls LaunchNext() so that the
+// kernel after it may launch in turn.
+bool LaunchOverlap();
+
+template <typename... KArgs, typename... Args>
+void Launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+            Args... args) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = LaunchOverlap() ? 1 : 0;
+  // an error is left for CheckLaunch (cudaGetLastError), as with <<< >>>
+  (void)cudaLaunchKernelEx(&config, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------------------
 // Device side.
 
 // Block size of the ggml formats: 32 values per block.
 constexpr int kBlock = 32;
+
+// The two halves of programmatic dependent launch (see Launch above).
+__device__ __forceinline__ void LaunchWait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void LaunchNext() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
 
 // FP16 bit pattern -> F32 by integer decode.  Same mapping as the reference's
 // Fp16ToFloat (src/quant.cc:44-71), including subnormal normalisation and the

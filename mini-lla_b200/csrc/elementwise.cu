@@ -58,6 +58,8 @@ __device__ __forceinline__ float4 Apply4(const Op& op, const float4& a,
 template <typename Op, bool BINARY>
 __global__ void __launch_bounds__(kThreads)
     Vec4Kernel(const float4* a, const float4* b, float4* out, int64_t n4) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const Op op;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(kThreads)
 template <typename Op, bool BINARY>
 __global__ void __launch_bounds__(kThreads)
     ScalarKernel(const float* a, const float* b, float* out, int64_t n) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const Op op;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -84,6 +88,8 @@ __global__ void __launch_bounds__(kThreads)
 __global__ void __launch_bounds__(kThreads)
     AddBiasVec4Kernel(const float4* value, const float4* bias, float4* out,
                       int64_t rows, int c4) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int64_t total = rows * c4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -97,6 +103,8 @@ __global__ void __launch_bounds__(kThreads)
 __global__ void __launch_bounds__(kThreads)
     AddBiasScalarKernel(const float* value, const float* bias, float* out,
                         int64_t rows, int64_t cols) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int64_t total = rows * cols;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -126,11 +134,10 @@ int LaunchElementwise(const char* name, const float* a, const float* b,
                    (!BINARY || Aligned16(b));
   if (vec) {
     const int64_t n4 = n / 4;
-    Vec4Kernel<Op, BINARY><<<GridFor(n4), kThreads, 0, s>>>(
-        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),
+    Launch(Vec4Kernel<Op, BINARY>, GridFor(n4), kThreads, 0, s, reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),
         reinterpret_cast<float4*>(out), n4);
   } else {
-    ScalarKernel<Op, BINARY><<<GridFor(n), kThreads, 0, s>>>(a, b, out, n);
+    Launch(ScalarKernel<Op, BINARY>, GridFor(n), kThreads, 0, s, a, b, out, n);
   }
   return CheckLaunch(name);
 }
@@ -178,13 +185,11 @@ int mlb_add_bias_f32(const float* value, const float* bias, float* out,
                    (bias == nullptr || Aligned16(bias));
   if (vec) {
     const int c4 = static_cast<int>(cols / 4);
-    AddBiasVec4Kernel<<<GridFor(rows * c4), kThreads, 0, s>>>(
-        reinterpret_cast<const float4*>(value),
+    Launch(AddBiasVec4Kernel, GridFor(rows * c4), kThreads, 0, s, reinterpret_cast<const float4*>(value),
         reinterpret_cast<const float4*>(bias), reinterpret_cast<float4*>(out),
         rows, c4);
   } else {
-    AddBiasScalarKernel<<<GridFor(rows * cols), kThreads, 0, s>>>(
-        value, bias, out, rows, cols);
+    Launch(AddBiasScalarKernel, GridFor(rows * cols), kThreads, 0, s, value, bias, out, rows, cols);
   }
   return CheckLaunch("mlb_add_bias_f32");
 }

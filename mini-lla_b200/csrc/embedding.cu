@@ -137,6 +137,8 @@ template <int QT>
 __global__ void __launch_bounds__(256) EmbeddingStagedKernel(EmbArgs a,
                                                              int64_t table_bytes,
                                                              int per_cta) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   extern __shared__ __align__(16) uint8_t staged[];
   constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
   const int groups = a.cols >> 2;
@@ -179,6 +181,8 @@ template <int QT>
 __global__ void __launch_bounds__(256) EmbeddingStagedWarpKernel(EmbArgs a,
                                                                  int64_t table_bytes,
                                                                  int slice) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   extern __shared__ __align__(16) uint8_t staged[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -209,6 +213,8 @@ __global__ void __launch_bounds__(256) EmbeddingStagedWarpKernel(EmbArgs a,
 
 // F32 tables with 16-byte aligned rows: a plain row copy, one CTA per token.
 __global__ void __launch_bounds__(256) EmbeddingF32Kernel(EmbArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int groups = a.cols >> 2;
   for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
     const int32_t token = a.tokens != nullptr ? __ldg(a.tokens + t) : a.token;
@@ -246,6 +252,8 @@ __device__ __forceinline__ float DecodeOne(int qt, const uint8_t* row, int i) {
 }
 
 __global__ void __launch_bounds__(256) EmbeddingScalarKernel(EmbArgs a, int qt) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
     const int32_t token = a.tokens != nullptr ? a.tokens[t] : a.token;
     float* out = a.out + static_cast<size_t>(t) * a.cols;
@@ -306,7 +314,7 @@ int LaunchEmbedding(const void* table, int qtype, int64_t vocab, int64_t cols,
   const int64_t smem = (per_cta / 8 * bb + 15 + 15) / 16 * 16;
   const int64_t table_bytes_all = vocab * row_bytes;
   if (vec && qtype == MLB_F32 && (tbl & 15u) == 0) {
-    EmbeddingF32Kernel<<<grid, threads, 0, s>>>(a);
+    Launch(EmbeddingF32Kernel, grid, threads, 0, s, a);
   } else if (vec && qtype != MLB_F32 &&
              (cols <= 1024 || (rows >= fill && row_bytes <= kWarpRowBytes))) {
     // warp per row; 8 rows per CTA unless rows are too few to fill the SMs
@@ -319,13 +327,13 @@ int LaunchEmbedding(const void* table, int qtype, int64_t vocab, int64_t cols,
     const size_t shm = static_cast<size_t>(slice) * wpc;
     switch (qtype) {
       case MLB_Q8_0:
-        EmbeddingStagedWarpKernel<MLB_Q8_0><<<wgrid, wthreads, shm, s>>>(a, table_bytes_all, slice);
+        Launch(EmbeddingStagedWarpKernel<MLB_Q8_0>, wgrid, wthreads, shm, s, a, table_bytes_all, slice);
         break;
       case MLB_Q4_0:
-        EmbeddingStagedWarpKernel<MLB_Q4_0><<<wgrid, wthreads, shm, s>>>(a, table_bytes_all, slice);
+        Launch(EmbeddingStagedWarpKernel<MLB_Q4_0>, wgrid, wthreads, shm, s, a, table_bytes_all, slice);
         break;
       case MLB_Q4_1:
-        EmbeddingStagedWarpKernel<MLB_Q4_1><<<wgrid, wthreads, shm, s>>>(a, table_bytes_all, slice);
+        Launch(EmbeddingStagedWarpKernel<MLB_Q4_1>, wgrid, wthreads, shm, s, a, table_bytes_all, slice);
         break;
     }
   } else if (vec && qtype != MLB_F32 && smem <= kMaxStagedBytes) {
@@ -337,17 +345,17 @@ int LaunchEmbedding(const void* table, int qtype, int64_t vocab, int64_t cols,
     const int pc = static_cast<int>(per_cta);
     switch (qtype) {
       case MLB_Q8_0:
-        EmbeddingStagedKernel<MLB_Q8_0><<<grid2, cta_threads, shm, s>>>(a, table_bytes, pc);
+        Launch(EmbeddingStagedKernel<MLB_Q8_0>, grid2, cta_threads, shm, s, a, table_bytes, pc);
         break;
       case MLB_Q4_0:
-        EmbeddingStagedKernel<MLB_Q4_0><<<grid2, cta_threads, shm, s>>>(a, table_bytes, pc);
+        Launch(EmbeddingStagedKernel<MLB_Q4_0>, grid2, cta_threads, shm, s, a, table_bytes, pc);
         break;
       case MLB_Q4_1:
-        EmbeddingStagedKernel<MLB_Q4_1><<<grid2, cta_threads, shm, s>>>(a, table_bytes, pc);
+        Launch(EmbeddingStagedKernel<MLB_Q4_1>, grid2, cta_threads, shm, s, a, table_bytes, pc);
         break;
     }
   } else {
-    EmbeddingScalarKernel<<<grid, 256, 0, s>>>(a, qtype);
+    Launch(EmbeddingScalarKernel, grid, 256, 0, s, a, qtype);
   }
   return CheckLaunch(op);
 }

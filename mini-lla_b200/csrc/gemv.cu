@@ -99,6 +99,8 @@ __device__ __forceinline__ float Dot4(const float4& a, const float4& b, float ac
 // Chunk c + 1 is copied in (cp.async) while chunk c is computed.
 template <int QT, int T>
 __global__ void __launch_bounds__(256) GemvKernel(GemvArgs a, int slice) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int kBB = QT == MLB_Q8_0 ? 34 : (QT == MLB_Q4_0 ? 18 : 20);
   const int lane = threadIdx.x & 31;
@@ -413,6 +415,8 @@ __device__ __forceinline__ void BulkGroup8(const uint8_t* blk, const float4* xa,
 template <int QT, int T>
 __global__ void __launch_bounds__(kBulkMaxWarps * 32, 1)
     GemvBulkKernel(GemvArgs a, int sb, int slot_bytes) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int kBB = BlockBytes<QT>();
   const int lane = threadIdx.x & 31;
@@ -549,6 +553,8 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32, 1)
 // sequential sum of dequant(w_i) * x_i (cuda_matmul.cu:41-101 shape).
 __global__ void __launch_bounds__(256)
     GemvScalarKernel(GemvArgs a, int qt, int64_t t_rows) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int64_t total = t_rows * a.n;
   const int bb = qt == MLB_Q8_0 ? 34 : (qt == MLB_Q4_0 ? 18 : 20);
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -609,7 +615,7 @@ int LaunchBulk(const GemvArgs& a, int warps, int sb, int slot, cudaStream_t s) {
   int64_t blocks = static_cast<int64_t>(per_sm) * SmCount();
   const int64_t needed = (a.n + warps - 1) / warps;  // at least a row per warp
   if (blocks > needed) blocks = needed;
-  kernel<<<static_cast<unsigned>(blocks), warps * 32, shm, s>>>(a, sb, slot);
+  Launch(kernel, static_cast<unsigned>(blocks), warps * 32, shm, s, a, sb, slot);
   return CheckLaunch("mlb_linear_f32");
 }
 
@@ -648,7 +654,7 @@ int LaunchVec(const GemvArgs& a, int t_rows, bool bulk_ok, cudaStream_t s) {
   case N:                                                            \
     if (!AllowSmem(GemvKernel<QT, N>, shm))                          \
       return Fail(MLB_ERR_CUDA, "mlb_linear_f32: shared memory opt-in"); \
-    GemvKernel<QT, N><<<grid, 256, shm, s>>>(a, slice);              \
+    Launch(GemvKernel<QT, N>, grid, 256, shm, s, a, slice);              \
     break;
     MLB_T(1) MLB_T(2) MLB_T(3) MLB_T(4) MLB_T(5) MLB_T(6) MLB_T(7) MLB_T(8)
 #undef MLB_T
@@ -754,8 +760,7 @@ extern "C" int mlb_linear_f32(const void* w, int qtype, int64_t n, int64_t k,
                n * row_bytes, x, y};
     const int64_t total = n * t_rows;
     const int64_t blocks = (total + 255) / 256;
-    GemvScalarKernel<<<static_cast<unsigned>(blocks < 65535 * 64 ? blocks : 65535 * 64),
-                       256, 0, s>>>(a, qtype, t_rows);
+    Launch(GemvScalarKernel, static_cast<unsigned>(blocks < 65535 * 64 ? blocks : 65535 * 64), 256, 0, s, a, qtype, t_rows);
     return CheckLaunch("mlb_linear_f32");
   }
   // wide ggml matrices: int8 tensor cores, kGemvTcTokens tokens per pass

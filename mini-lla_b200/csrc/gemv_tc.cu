@@ -452,6 +452,8 @@ namespace {
 
 template <int QT, int T>  // T: tokens this instance computes (1, 2 or 4; a.tokens <= T)
 __global__ void __launch_bounds__(kGtThreads, 1) GemvTcKernel(const __grid_constant__ GtArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   constexpr int SB = GtStageBlocks(QT);
   constexpr int CPS = SB / kGtChunk;  // chunks per stage (1 or 2)
   constexpr int N = GtN(T);
@@ -872,11 +874,13 @@ int LaunchGemvTc(int count, const void* const* w, const int64_t* n, int64_t k, c
   cfg.blockDim = dim3(kGtThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(shm);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(split);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see Launch
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // persistent clusters: as many as fit on the GPU at once (one CTA per SM),
@@ -893,6 +897,7 @@ int LaunchGemvTc(int count, const void* const* w, const int64_t* n, int64_t k, c
   }
   const int clusters = fit < tiles ? fit : tiles;
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * split));
+  cfg.numAttrs = LaunchOverlap() ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kernel, a) != cudaSuccess) {
     cudaGetLastError();
     return Fail(MLB_ERR_CUDA, "mlb_linear_f32: launch failed");

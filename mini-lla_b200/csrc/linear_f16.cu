@@ -328,6 +328,8 @@ namespace {
 template <int QT>
 __global__ void __launch_bounds__(kHfThreads, 1)
     LinearF16Kernel(const __grid_constant__ HfGroup grp) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   constexpr int kBB = HfBlockBytes(QT);
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw_addr = HfSmem(smem_raw);
@@ -544,6 +546,8 @@ __global__ void __launch_bounds__(kHfThreads, 1)
 __global__ void __launch_bounds__(256)
     SplitF16Kernel(const float* __restrict__ x, __half* __restrict__ xh, __half* __restrict__ xl,
                    float* __restrict__ row_scale, int k) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float red[8];
   __shared__ int bad_row;
   const int64_t t = blockIdx.x;
@@ -662,7 +666,7 @@ int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int6
   __half* xh = reinterpret_cast<__half*>(scratch);
   __half* xl = xh + k * t_rows;  // k % 64 == 0: still 16-byte aligned
   float* row_scale = reinterpret_cast<float*>(xl + k * t_rows);
-  SplitF16Kernel<<<static_cast<unsigned>(t_rows), 256, 0, s>>>(x, xh, xl, row_scale,
+  Launch(SplitF16Kernel, static_cast<unsigned>(t_rows), 256, 0, s, x, xh, xl, row_scale,
                                                               static_cast<int>(k));
   int rc = CheckLaunch("mlb_linear_rows_f32");
   if (rc != MLB_OK) return rc;
@@ -682,7 +686,7 @@ int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int6
     cudaGetLastError();
     return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: shared memory opt-in");
   }
-  kernel<<<static_cast<unsigned>(tiles), kHfThreads, kHfSmemBytes, s>>>(grp);
+  Launch(kernel, static_cast<unsigned>(tiles), kHfThreads, kHfSmemBytes, s, grp);
   return CheckLaunch("mlb_linear_rows_f32");
 }
 

@@ -342,6 +342,8 @@ struct TcGroup {
 template <int QT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     LinearTcKernel(const __grid_constant__ TcGroup grp) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   constexpr int S = TcStages(QT);
   constexpr int kRaw = TcRawBytes(QT);
   constexpr int kBB = TcBlockBytes(QT);
@@ -520,6 +522,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 __global__ void __launch_bounds__(256)
     SplitTf32Kernel(const float4* __restrict__ x, uint4* __restrict__ xh,
                     uint4* __restrict__ xl, int64_t count4) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= count4) return;
   const float4 v = x[i];
@@ -603,7 +607,7 @@ int LaunchTc(int count, const void* const* w, const int64_t* n, int64_t k, int64
     cudaGetLastError();
     return Fail(MLB_ERR_CUDA, "mlb_linear_rows_f32: shared memory opt-in");
   }
-  kernel<<<static_cast<unsigned>(tiles), kTcThreads, shm, s>>>(grp);
+  Launch(kernel, static_cast<unsigned>(tiles), kTcThreads, shm, s, grp);
   return CheckLaunch("mlb_linear_rows_f32");
 }
 
@@ -715,8 +719,7 @@ int LinearRowsGroup(int count, const void* const* w, int qtype, const int64_t* n
   if (LinearF16Eligible(qtype, k, row_bytes))
     return LinearF16(used, ws, qtype, ns, k, row_bytes, x, t_rows, ys, xh, s);
   const int64_t count4 = k * t_rows / 4;
-  SplitTf32Kernel<<<static_cast<unsigned>((count4 + 255) / 256), 256, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(xh),
+  Launch(SplitTf32Kernel, static_cast<unsigned>((count4 + 255) / 256), 256, 0, s, reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(xh),
       reinterpret_cast<uint4*>(xl), count4);
   const int rc = CheckLaunch("mlb_linear_rows_f32");
   if (rc != MLB_OK) return rc;

@@ -70,6 +70,8 @@ __device__ __forceinline__ float SumSq(const float4& v, float acc) {
 
 template <int NV, bool RES>
 __global__ void __launch_bounds__(256) RmsNormWarpKernel(RmsArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int c4 = a.cols >> 2;
@@ -115,6 +117,8 @@ __global__ void __launch_bounds__(256) RmsNormWarpKernel(RmsArgs a) {
 
 template <int NV, bool RES>
 __global__ void __launch_bounds__(1024) RmsNormBlockKernel(RmsArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float scratch[2][32];
   const int c4 = a.cols >> 2;
   const float4* w4 = reinterpret_cast<const float4*>(a.w);
@@ -163,6 +167,8 @@ __global__ void __launch_bounds__(1024) RmsNormBlockKernel(RmsArgs a) {
 // thread.  The partial sums are combined in rank order (deterministic).
 template <int NV, bool RES>
 __global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float scratch[32];
@@ -218,6 +224,8 @@ __global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk
 
 template <bool RES>
 __global__ void __launch_bounds__(256) RmsNormScalarKernel(RmsArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float scratch[2][32];
   int parity = 0;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
@@ -271,7 +279,7 @@ int LaunchWarp(const RmsArgs& a, int nv, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(blocks < kMaxGrid ? blocks : kMaxGrid));
   switch (nv) {
 #define MLB_CASE(N) \
-  case N: RmsNormWarpKernel<N, RES><<<grid, threads, 0, s>>>(a); break;
+  case N: Launch(RmsNormWarpKernel<N, RES>, grid, threads, 0, s, a); break;
     MLB_CASE(1) MLB_CASE(2) MLB_CASE(3) MLB_CASE(4)
     MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
@@ -285,7 +293,7 @@ int LaunchBlock(const RmsArgs& a, int nv, int threads, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(a.rows < kMaxGrid ? a.rows : kMaxGrid));
   switch (nv) {
 #define MLB_CASE(N) \
-  case N: RmsNormBlockKernel<N, RES><<<grid, threads, 0, s>>>(a); break;
+  case N: Launch(RmsNormBlockKernel<N, RES>, grid, threads, 0, s, a); break;
     MLB_CASE(1) MLB_CASE(2) MLB_CASE(3) MLB_CASE(4)
     MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
@@ -308,13 +316,15 @@ int LaunchCluster(const RmsArgs& a, int ranks, cudaStream_t s) {
   config.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   config.dynamicSmemBytes = 0;
   config.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = static_cast<unsigned>(ranks);
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see Launch
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attr;
-  config.numAttrs = 1;
+  config.numAttrs = LaunchOverlap() ? 2 : 1;
   cudaError_t err = cudaErrorInvalidValue;
   switch (nv) {
     case 1: err = cudaLaunchKernelEx(&config, RmsNormClusterKernel<1, RES>, a, chunk); break;
@@ -333,7 +343,7 @@ int LaunchCluster(const RmsArgs& a, int ranks, cudaStream_t s) {
 template <bool RES>
 int LaunchScalar(const RmsArgs& a, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(a.rows < kMaxGrid ? a.rows : kMaxGrid));
-  RmsNormScalarKernel<RES><<<grid, 256, 0, s>>>(a);
+  Launch(RmsNormScalarKernel<RES>, grid, 256, 0, s, a);
   return CheckLaunch("mlb_rmsnorm_f32");
 }
 

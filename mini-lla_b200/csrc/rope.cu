@@ -64,6 +64,8 @@ __device__ __forceinline__ void Rotate(float& x0, float& x1, float c, float s) {
 // and the extra index registers of the split form cost 2 of 8 CTAs per SM.
 template <bool NEOX, bool SPLIT>
 __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int half = a.hd >> 1;
   const int groups = NEOX ? (a.hd >> 3) : (a.hd >> 2);  // per head
   const int items = (a.nq + a.nk) * groups;
@@ -123,6 +125,8 @@ __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
 
 // Any even hd / alignment: one item per rotated pair.
 __global__ void __launch_bounds__(256) RopeScalarKernel(RopeArgs a, int neox) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int half = a.hd >> 1;
   const int heads = a.nq + a.nk;
   const int items = heads * half;
@@ -197,14 +201,14 @@ extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
     if (split > max_split) split = max_split;
     const dim3 grid2(grid.x, static_cast<unsigned>(split));
     if (split > 1) {
-      if (neox) RopeVecKernel<true, true><<<grid2, threads, 0, s>>>(a);
-      else RopeVecKernel<false, true><<<grid2, threads, 0, s>>>(a);
+      if (neox) Launch(RopeVecKernel<true, true>, grid2, threads, 0, s, a);
+      else Launch(RopeVecKernel<false, true>, grid2, threads, 0, s, a);
     } else {
-      if (neox) RopeVecKernel<true, false><<<grid, threads, 0, s>>>(a);
-      else RopeVecKernel<false, false><<<grid, threads, 0, s>>>(a);
+      if (neox) Launch(RopeVecKernel<true, false>, grid, threads, 0, s, a);
+      else Launch(RopeVecKernel<false, false>, grid, threads, 0, s, a);
     }
   } else {
-    RopeScalarKernel<<<grid, 256, 0, s>>>(a, neox);
+    Launch(RopeScalarKernel, grid, 256, 0, s, a, neox);
   }
   return CheckLaunch("mlb_rope_f32");
 }

@@ -14,7 +14,11 @@ thread_local std::string g_last_error;
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];
 
+std::atomic<int> g_launch_overlap{1};
+
 }  // namespace
+
+bool LaunchOverlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
 
 void SetError(const std::string& message) { g_last_error = message; }
 
@@ -53,6 +57,14 @@ int SmCount() {
 extern "C" {
 
 int mlb_version(void) { return 100; }
+
+int mlb_set_launch_overlap(int on) {
+  if (on != 0 && on != 1) return mlb::Fail(MLB_ERR_ARG, "mlb_set_launch_overlap: on must be 0 or 1");
+  mlb::g_launch_overlap.store(on, std::memory_order_relaxed);
+  return MLB_OK;
+}
+
+int mlb_launch_overlap(void) { return mlb::LaunchOverlap() ? 1 : 0; }
 
 const char* mlb_last_error(void) { return mlb::g_last_error.c_str(); }
 

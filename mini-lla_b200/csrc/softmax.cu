@@ -75,6 +75,8 @@ __device__ __forceinline__ float4 Div4(const float4& e, float total, int i4,
 
 template <int NV>
 __global__ void __launch_bounds__(256) SoftmaxWarpKernel(SoftmaxArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int c4 = a.cols >> 2;
@@ -119,6 +121,8 @@ __global__ void __launch_bounds__(256) SoftmaxWarpKernel(SoftmaxArgs a) {
 
 template <int NV>
 __global__ void __launch_bounds__(1024) SoftmaxBlockKernel(SoftmaxArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float scratch[2][32];
   const int c4 = a.cols >> 2;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
@@ -163,6 +167,8 @@ __global__ void __launch_bounds__(1024) SoftmaxBlockKernel(SoftmaxArgs a) {
 }
 
 __global__ void __launch_bounds__(256) SoftmaxScalarKernel(SoftmaxArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
   __shared__ float scratch[2][32];
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     bool bad;
@@ -217,7 +223,7 @@ extern "C" int mlb_softmax_rows_f32(const float* x, float* y, int64_t rows,
     const dim3 grid(static_cast<unsigned>(blocks < kMaxGrid ? blocks : kMaxGrid));
     switch (nv) {
 #define MLB_CASE(N) \
-  case N: SoftmaxWarpKernel<N><<<grid, threads, 0, s>>>(a); break;
+  case N: Launch(SoftmaxWarpKernel<N>, grid, threads, 0, s, a); break;
       MLB_CASE(1) MLB_CASE(2) MLB_CASE(3) MLB_CASE(4)
       MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
@@ -232,13 +238,13 @@ extern "C" int mlb_softmax_rows_f32(const float* x, float* y, int64_t rows,
     threads = (threads + 31) / 32 * 32;
     switch (nv) {
 #define MLB_CASE(N) \
-  case N: SoftmaxBlockKernel<N><<<grid, threads, 0, s>>>(a); break;
+  case N: Launch(SoftmaxBlockKernel<N>, grid, threads, 0, s, a); break;
       MLB_CASE(1) MLB_CASE(2) MLB_CASE(3) MLB_CASE(4)
       MLB_CASE(5) MLB_CASE(6) MLB_CASE(7) MLB_CASE(8)
 #undef MLB_CASE
     }
     return CheckLaunch("mlb_softmax_rows_f32");
   }
-  SoftmaxScalarKernel<<<grid, 256, 0, s>>>(a);
+  Launch(SoftmaxScalarKernel, grid, 256, 0, s, a);
   return CheckLaunch("mlb_softmax_rows_f32");
 }

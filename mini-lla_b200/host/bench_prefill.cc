@@ -9,6 +9,8 @@
 // needed.  Built by `make -C oracle dropin` next to the checks.
 #include <cuda_runtime.h>
 
+#include "mlb_ops.h"
+
 #include <chrono>
 #include <cstdint>
 #include <cstdio>
@@ -42,6 +44,7 @@ struct Args {
   int decode = 32;        // decode steps after the prompt (0: skip)
   int cpu_tokens = 2;     // tokens through the CPU forward pass (0: skip)
   int max_rows = 512;
+  int overlap = 1;        // programmatic dependent launch (mlb_set_launch_overlap)
 };
 
 uint16_t RandomScale(std::mt19937& rng) {
@@ -182,10 +185,15 @@ int main(int argc, char** argv) {
     else if (k == "--decode") a.decode = std::stoi(v);
     else if (k == "--cpu-tokens") a.cpu_tokens = std::stoi(v);
     else if (k == "--max-rows") a.max_rows = std::stoi(v);
+    else if (k == "--overlap") a.overlap = std::stoi(v);
     else {
       std::fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
     }
+  }
+  if (mlb_set_launch_overlap(a.overlap) != MLB_OK) {
+    std::fprintf(stderr, "--overlap takes 0 or 1\n");
+    return 2;
   }
   try {
     Model model = BuildModel(a);
@@ -267,10 +275,11 @@ int main(int argc, char** argv) {
         "\"decode_ms_per_token\": %.4f, \"decode_device_ms_per_token\": %.4f, "
         "\"per_token_driver_ms_per_token\": %.4f, "
         "\"cpu_ms_per_token\": %.2f, \"cpu_threads\": %u, \"cpu_tokens\": %d, "
-        "\"per_token_tokens\": %d}\n",
+        "\"per_token_tokens\": %d, \"launch_overlap\": %d}\n",
         a.vocab, a.dim, a.hidden, a.layers, a.heads, a.kv_heads, TypeName(a.type),
         a.tokens, prefill_s * 1e3, device_ms, a.tokens / prefill_s, decode_s * 1e3,
-        decode_device_ms, per_token_s * 1e3, cpu_s * 1e3, cores, a.cpu_tokens, std::min(a.per_token, a.tokens));
+        decode_device_ms, per_token_s * 1e3, cpu_s * 1e3, cores, a.cpu_tokens,
+        std::min(a.per_token, a.tokens), a.overlap);
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());
     return 1;

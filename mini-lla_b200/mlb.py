@@ -53,6 +53,8 @@ SIGNATURES = {
     "mlb_wait_timeouts": (c_int, [c_void_p]),
     "mlb_set_gemv_path": (c_int, [c_int]),
     "mlb_gemv_path": (c_int, []),
+    "mlb_set_launch_overlap": (c_int, [c_int]),
+    "mlb_launch_overlap": (c_int, []),
     "mlb_linear_rows_scratch_floats": (c_int64, [c_int64, c_int64]),
     "mlb_linear_rows_f32": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p,
                                     c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
@@ -476,6 +478,15 @@ def set_gemv_path(path: int) -> int:
     the previous setting."""
     previous = load().mlb_gemv_path()
     _check(load().mlb_set_gemv_path(int(path)), "set_gemv_path")
+    return previous
+
+
+def set_launch_overlap(on: int) -> int:
+    """1: kernels launch with programmatic dependent launch (each overlaps
+    the tail of the stream's previous kernel; the default), 0: one after
+    another.  Returns the previous setting."""
+    previous = load().mlb_launch_overlap()
+    _check(load().mlb_set_launch_overlap(int(on)), "set_launch_overlap")
     return previous
 
 

@@ -184,3 +184,21 @@ def test_gemv_path_switch():
         assert mlb.set_gemv_path(2) == 0 and mlb.set_gemv_path(0) == 2
     finally:
         lib.mlb_set_gemv_path(previous)
+
+
+def test_launch_overlap_switch():
+    """Programmatic dependent launch on / off (no GPU work): on by default,
+    0 / 1 taken and read back, anything else refused and the setting kept."""
+    lib = mlb.load()
+    previous = lib.mlb_launch_overlap()
+    try:
+        assert previous == 1
+        for on in (0, 1):
+            assert lib.mlb_set_launch_overlap(on) == 0
+            assert lib.mlb_launch_overlap() == on
+        for bad in (-1, 2):
+            assert lib.mlb_set_launch_overlap(bad) == 1  # MLB_ERR_ARG
+            assert lib.mlb_launch_overlap() == 1
+        assert mlb.set_launch_overlap(0) == 1 and mlb.set_launch_overlap(1) == 0
+    finally:
+        lib.mlb_set_launch_overlap(previous)
