@@ -20,6 +20,7 @@ flush is needed between steps.  Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import glob
 import json
 import subprocess
 import math
@@ -217,7 +218,54 @@ class LayerStep:
             events[len(self.ops)].record()
 
 
-def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
+def gpu_numa_cpus(device_index: int):
+    """CPUs of the NUMA node the GPU hangs off (from sysfs), or None when the
+    node is unknown or the host has a single node."""
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(device_index)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{bdf}/numa_node").read().strip())
+        if node < 0 or len(glob.glob("/sys/devices/system/node/node[0-9]*")) < 2:
+            return None
+        cpus = parse_cpulist(open(f"/sys/devices/system/node/node{node}/cpulist").read())
+        return node, cpus & os.sched_getaffinity(0)
+    except (OSError, ValueError, AttributeError, RuntimeError, AssertionError):
+        return None
+
+
+def parse_cpulist(text: str) -> set:
+    """sysfs cpulist ("0-15,32-47") -> set of CPU ids."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if part:
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def pinned_near_gpu(device_index: int, numa: bool):
+    """A context for allocating pinned host buffers: pages land on the node
+    of the allocating CPU, so the thread runs on the GPU's own NUMA node while
+    inside (its affinity is restored on exit).  Yields that node or None."""
+    import contextlib
+
+    @contextlib.contextmanager
+    def ctx():
+        found = gpu_numa_cpus(device_index) if numa else None
+        if not found or not found[1]:
+            yield None
+            return
+        before = os.sched_getaffinity(0)
+        os.sched_setaffinity(0, found[1])
+        try:
+            yield found[0]
+        finally:
+            os.sched_setaffinity(0, before)
+    return ctx()
+
+
+def e2e_run(step: LayerStep, steps: int, chunks: int = 8, numa: bool = True):
     """The same step end to end through the public API with host buffers:
     every step copies its inputs from pinned host memory, runs the
     operators, and reads every result back, pipelined over token chunks on
@@ -231,12 +279,14 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8):
         out_keys += ["probs"]
     in_keys = [k for k in in_keys if d.get(k) is not None]
     out_keys = [k for k in out_keys if d.get(k) is not None]
-    host_in = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
-               for k in in_keys}
-    host_out = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
-                for k in out_keys}
-    for k in in_keys:
-        host_in[k].copy_(d[k])
+    with pinned_near_gpu(step.dev.index or 0, numa) as node:
+        host_in = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
+                   for k in in_keys}
+        host_out = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
+                    for k in out_keys}
+        for k in in_keys:
+            host_in[k].copy_(d[k])
+    step.e2e_numa_node = node
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
     s_in, s_cmp, s_out = (torch.cuda.Stream() for _ in range(3))
@@ -578,7 +628,7 @@ def gpu_arm(args, cfg):
     if args.no_e2e:
         e2e_ms, h2d, d2h = float("nan"), 0, 0
     else:
-        e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps)
+        e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps, numa=bool(args.e2e_numa))
     stats = torch.tensor([total_ms, e2e_ms] + op_ms, dtype=torch.float64,
                          device=dev)
     if world > 1:
@@ -631,7 +681,8 @@ def gpu_arm(args, cfg):
         "e2e": None if args.no_e2e else {
             "value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3)},
+            "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3),
+            "pinned_numa_node": getattr(step, "e2e_numa_node", None)},
         "timing": "cuda graph replay" if use_graph else "direct launches",
         "launch_overlap": args.launch_overlap,
         "gpu_launches": args.steps * len(step.ops),
@@ -946,6 +997,8 @@ def main():
                     help="seconds of CPU work for the CPU legs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-numa", type=int, default=1, choices=(0, 1),
+                    help="1: allocate the pinned host buffers on the GPU's NUMA node")
     ap.add_argument("--ops", default="",
                     help="comma list: time only these operators of the step")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
