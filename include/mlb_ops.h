@@ -241,10 +241,11 @@ int64_t mlb_linear_rows_scratch_floats(int64_t k, int64_t t_rows);
  * reference's CudaLinear / Linear (cuda_matmul.cu, quant.cc:171-226) applied
  * to every token of a prompt at once.  From 48 tokens on (k % 32 == 0,
  * row_bytes % 16 == 0, 16-byte aligned table and x) it runs on the tensor
- * cores.  Q8_0 / Q4_0 (k % 64 == 0): the codes are exact fp16 MMA operands
- * and x, scaled per token by a power of two, is split into two fp16 pieces;
- * every ggml block's sum lands in its own fp32 accumulator and the block
- * scale is applied outside the tensor core.  Q4_1 / F32: tcgen05 TF32 MMAs
+ * cores.  Q8_0 / Q4_0 (k % 64 == 0): each dequantised weight d * q is split
+ * into two fp16 pieces without error (|d| < 512; a 128 x 128 tile with a
+ * larger or non-finite block scale is computed on the CUDA cores), x,
+ * scaled per token by a power of two, into two fp16 pieces, and one fp32
+ * accumulator spans the whole of k.  Q4_1 / F32: tcgen05 TF32 MMAs
  * with W dequantised and both operands split into TF32 head + tail (three
  * products per tile).  Either way the result stays within 1e-5 * sum|w x|
  * of the reference's fp32 sum; `scratch` (caller-owned device memory of

@@ -715,7 +715,7 @@ int LinearRowsGroup(int count, const void* const* w, int qtype, const int64_t* n
   float* xh = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(scratch) + 15) & ~uintptr_t{15});
   float* xl = xh + k * t_rows;  // k % 32 == 0: still 16-byte aligned
   cudaStream_t s = AsStream(stream);
-  // Q8_0 / Q4_0: the codes are exact fp16 operands (linear_f16.cu)
+  // Q8_0 / Q4_0: d * q and x in exact fp16 pieces (linear_f16.cu)
   if (LinearF16Eligible(qtype, k, row_bytes))
     return LinearF16(used, ws, qtype, ns, k, row_bytes, x, t_rows, ys, xh, s);
   const int64_t count4 = k * t_rows / 4;
