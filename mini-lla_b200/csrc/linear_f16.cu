@@ -600,6 +600,70 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same split with the row held in registers (NV float4 per thread of
+// 512, rows of up to 16384 values): x is read once.
+template <int NV>
+__global__ void __launch_bounds__(512)
+    SplitF16RegKernel(const float* __restrict__ x, __half* __restrict__ xh,
+                      __half* __restrict__ xl, float* __restrict__ row_scale, int k) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
+  __shared__ float red[16];
+  __shared__ int bad_row;
+  const int64_t t = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + t * k);
+  const int k4 = k >> 2;
+  float4 v[NV];
+  float mx = 0.0f;
+  int bad = 0;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = static_cast<int>(threadIdx.x) + 512 * j;
+    v[j] = i < k4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    bad |= !(fabsf(v[j].x) <= 3.402823466e38f) | !(fabsf(v[j].y) <= 3.402823466e38f) |
+           !(fabsf(v[j].z) <= 3.402823466e38f) | !(fabsf(v[j].w) <= 3.402823466e38f);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  bad = __any_sync(0xffffffffu, bad);
+  if (threadIdx.x == 0) bad_row = 0;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x >> 5] = mx;
+    if (bad) bad_row = 1;
+  }
+  __syncthreads();
+  mx = red[0];
+  for (int i = 1; i < 16; ++i) mx = fmaxf(mx, red[i]);
+  // as SplitF16Kernel: s = 2^(e - 15) with mx < 2^e, e kept >= -111
+  int e = 0;
+  frexpf(mx, &e);
+  e = e < -111 ? -111 : e;
+  const bool plain = bad_row || mx == 0.0f;
+  const float inv = plain ? 1.0f : ldexpf(1.0f, 15 - e);
+  if (threadIdx.x == 0) row_scale[t] = plain ? 1.0f : ldexpf(1.0f, e - 15);
+  __half2* h2 = reinterpret_cast<__half2*>(xh + t * k);
+  __half2* l2 = reinterpret_cast<__half2*>(xl + t * k);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = static_cast<int>(threadIdx.x) + 512 * j;
+    if (i < k4) {
+      const float a[4] = {v[j].x * inv, v[j].y * inv, v[j].z * inv, v[j].w * inv};  // exact
+      __half hi[4], lo[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        hi[q] = __float2half_rn(a[q]);
+        lo[q] = __float2half_rn(a[q] - __half2float(hi[q]));  // exact remainder
+      }
+      h2[2 * i] = __halves2half2(hi[0], hi[1]);
+      h2[2 * i + 1] = __halves2half2(hi[2], hi[3]);
+      l2[2 * i] = __halves2half2(lo[0], lo[1]);
+      l2[2 * i + 1] = __halves2half2(lo[2], lo[3]);
+    }
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 HfEncodeFn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -666,8 +730,19 @@ int LinearF16(int count, const void* const* w, int qtype, const int64_t* n, int6
   __half* xh = reinterpret_cast<__half*>(scratch);
   __half* xl = xh + k * t_rows;  // k % 64 == 0: still 16-byte aligned
   float* row_scale = reinterpret_cast<float*>(xl + k * t_rows);
-  Launch(SplitF16Kernel, static_cast<unsigned>(t_rows), 256, 0, s, x, xh, xl, row_scale,
-                                                              static_cast<int>(k));
+  switch ((k / 4 + 511) / 512) {  // float4 per thread of 512
+    case 1: Launch(SplitF16RegKernel<1>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 2: Launch(SplitF16RegKernel<2>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 3: Launch(SplitF16RegKernel<3>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 4: Launch(SplitF16RegKernel<4>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 5: Launch(SplitF16RegKernel<5>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 6: Launch(SplitF16RegKernel<6>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 7: Launch(SplitF16RegKernel<7>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    case 8: Launch(SplitF16RegKernel<8>, static_cast<unsigned>(t_rows), 512, 0, s, x, xh, xl, row_scale, static_cast<int>(k)); break;
+    default:  // longer rows: two passes over x
+      Launch(SplitF16Kernel, static_cast<unsigned>(t_rows), 256, 0, s, x, xh, xl, row_scale,
+             static_cast<int>(k));
+  }
   int rc = CheckLaunch("mlb_linear_rows_f32");
   if (rc != MLB_OK) return rc;
   if (!HfMap2D(&grp.x[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, static_cast<uint64_t>(k),
