@@ -852,8 +852,9 @@ SWEEP_OPS = ("rmsnorm", "res_rmsnorm", "swiglu", "emb_q8_0", "emb_q4_0", "emb_q4
 
 
 def sweep(args):
-    """Bandwidth sweep: every operator x hidden size x token
-    count, seed 1, quant tables of 32000 rows; one JSON line per point with
+    """Bandwidth sweep: every operator (RMSNorm, residual RMSNorm, SwiGLU,
+    Q8_0 / Q4_0 / Q4_1 gather) x hidden size {512 .. 16384} x token count
+    {1 .. 262144}, seed 1, quant tables of 32000 rows; one JSON line per point with
     GB/s per GPU and the fractions of the measured and spec peaks.  Weak
     scaling under torchrun: every rank runs the point on its own GPU and the
     slowest rank's time is reported."""
