@@ -10,9 +10,10 @@ LLaMA-3-8B-shaped prefill (T = 16384 token rows per GPU, hidden 4096, FFN
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
     python bench.py --impl reference ...   # the reference's CPU operators
 
-For N > 1 launch one process per GPU with torch.distributed.run; every rank
-owns its own contiguous block of token rows (weak scaling: T rows per GPU)
-and the data path has no collective.  Timing: W untimed steps, then K steps
+For N > 1 launch one process per GPU with torch.distributed.run; the
+workload's T token rows are split into N contiguous ranges, one per rank
+(strong scaling: the split the sharded prefill workloads name; `--weak` gives
+every rank its own T rows instead), and the data path has no collective.  Timing: W untimed steps, then K steps
 between a barrier + synchronize on both sides, CUDA events on the launching
 stream, max over ranks.  Inputs are far larger than the 126 MB L2, so no
 flush is needed between steps.  Rank 0 prints one JSON line.
@@ -517,22 +518,29 @@ def run_cpu(cfg, steps: int, warmup: int, budget_s: float):
     sample = CpuLayerSample(cfg, rows)
     for _ in range(warmup):
         sample.step()
+    per_step = []
     t0 = time.perf_counter()
     for _ in range(steps):
+        t1 = time.perf_counter()
         sample.step()
+        per_step.append(time.perf_counter() - t1)
     sec = (time.perf_counter() - t0) / steps
+    rates = sorted(rows / s for s in per_step)
     ops_bytes = (cfg.bytes_embedding(rows) + cfg.bytes_rmsnorm(rows) +
                  cfg.bytes_rope(rows) + cfg.bytes_swiglu(rows))
     return {"tokens_per_s": rows / sec, "gbs": ops_bytes / sec / 1e9,
             "rows": rows, "sec_per_step": sec, "kind": sample.kind,
-            "cores": sample.cores}
+            "cores": sample.cores, "steps": steps, "warmup": warmup,
+            "spread": {"min": round(rates[0], 1),
+                       "median": round(statistics.median(rates), 1),
+                       "max": round(rates[-1], 1)}}
 
 
 def reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    warm = max(1, min(args.warmup, 3))
+    warm = max(1, args.warmup)
     res = run_cpu(cfg, args.steps, warm, budget_s=args.cpu_budget)
     sample = (f"{res['rows']} of {cfg.tokens} token rows of {cfg.name} per step "
               f"(embedding, {'residual ' if cfg.residual else ''}RMSNorm, RoPE, "
@@ -548,7 +556,7 @@ def reference_arm(args, cfg):
         "hbm_gbs_equiv": round(res["gbs"], 2),
         "cpu_baseline": {"value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
                          "cores": res["cores"], "kind": res["kind"],
-                         "sample": sample},
+                         "sample": sample, "spread_tokens_per_s": res["spread"]},
         "e2e": {"value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -556,10 +564,10 @@ def reference_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-def config_block(cfg, args, tokens_per_gpu):
+def config_block(cfg, args, tokens_per_gpu, global_tokens):
     return {
         "workload": cfg.name, "tokens_per_gpu": tokens_per_gpu,
-        "global_tokens": tokens_per_gpu * args.gpus, "hidden": cfg.hidden,
+        "global_tokens": global_tokens, "hidden": cfg.hidden,
         "ffn": cfg.ffn, "heads": cfg.n_heads, "kv_heads": cfg.n_kv_heads,
         "head_dim": cfg.head_dim, "rope": "neox" if cfg.neox else "normal",
         "rope_theta": cfg.theta, "qk_bias": cfg.bias,
@@ -587,14 +595,15 @@ def gpu_arm(args, cfg):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    # weak scaling: every GPU owns a block of cfg.tokens rows (positions of a
-    # sequence each); --strong splits one batch of cfg.tokens rows instead.
+    # strong scaling (default): one batch of cfg.tokens rows — a sequence at
+    # positions 0..T-1 — split into contiguous token ranges, one per rank;
+    # --weak gives every rank its own block of cfg.tokens rows.
     total_tokens = args.tokens or cfg.tokens
-    if args.strong:
+    if args.weak:
+        tokens, pos_offset = total_tokens, 0
+    else:
         r0, r1 = wl.shard_range(total_tokens, world, rank)
         tokens, pos_offset = r1 - r0, r0
-    else:
-        tokens, pos_offset = total_tokens, 0
     ops = args.ops.split(",") if args.ops else None
     step = LayerStep(cfg, dev, tokens, pos_offset, ops)
     nops = len(step.ops)
@@ -638,14 +647,16 @@ def gpu_arm(args, cfg):
     clocks = sampler.summary()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and ops is None:
-        cpu = run_cpu(cfg, 3, 1, budget_s=args.cpu_budget / 2)
+        # the same steps, warm-up and time budget as the reference arm
+        # (`--impl reference`), so both sample the same rows per step
+        cpu = run_cpu(cfg, args.steps, max(1, args.warmup), budget_s=args.cpu_budget)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
     ms_step = total_ms / args.steps
-    tokens_all = tokens * world
+    tokens_all = tokens * world if args.weak else total_tokens
     value = tokens_all / (ms_step / 1e3)
     step_bytes = sum(op_bytes.values())
     peak, peak_kind = measured_peak()
@@ -664,9 +675,9 @@ def gpu_arm(args, cfg):
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-        "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": config_block(cfg, args, tokens),
+        "config": config_block(cfg, args, tokens, tokens_all),
         "hbm_gbs": round(gbs_per_gpu * world, 1),
         "hbm_gbs_per_gpu": round(gbs_per_gpu, 1),
         "hbm_frac_of_measured": round(gbs_per_gpu / peak, 4),
@@ -691,7 +702,9 @@ def gpu_arm(args, cfg):
         line["cpu_baseline"] = {
             "value": round(cpu["tokens_per_s"], 1), "unit": "tokens/s",
             "cores": cpu["cores"], "kind": cpu["kind"],
-            "sample": f"{cpu['rows']} of {cfg.tokens} token rows per step, 3 steps"}
+            "sample": f"{cpu['rows']} of {cfg.tokens} token rows per step, "
+                      f"{cpu['steps']} steps after {cpu['warmup']} warm-up",
+            "spread_tokens_per_s": cpu["spread"]}
     print(json.dumps(line), flush=True)
 
 
@@ -991,8 +1004,9 @@ def main():
     ap.add_argument("--workload", default="llama3-8b-t16384",
                     choices=sorted(wl.CONFIGS))
     ap.add_argument("--impl", default="mlb", choices=["mlb", "reference"])
-    ap.add_argument("--strong", action="store_true",
-                    help="split one batch of T rows across GPUs")
+    ap.add_argument("--weak", action="store_true",
+                    help="every GPU runs its own T rows (default: the T rows "
+                         "are split across the GPUs)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=20.0,
                     help="seconds of CPU work for the CPU legs")

@@ -347,6 +347,33 @@ def test_embedding_bad_tokens_flagged(cuda, oracle):
     assert_bitexact(out[[0, 3]], want)
 
 
+@pytest.mark.parametrize("qtype,offset", [(wl.Q8_0, 2), (wl.Q8_0, 14), (wl.Q4_0, 6),
+                                          (wl.Q4_1, 4), (wl.Q4_1, 12)])
+@pytest.mark.parametrize("cols,T", [(896, 3000), (4096, 77), (4096, 3000), (40000, 5)])
+def test_embedding_table_not_16_byte_aligned(cuda, oracle, qtype, offset, cols, T):
+    """A table that is only 2-byte (Q8_0, Q4_0) or 4-byte (Q4_1) aligned, as
+    the C ABI allows: staged windows then start before the table or end past
+    it, and only the table's own bytes may be read.  Covers the warp-per-row,
+    two-rows-per-CTA, split-row (few tokens) and long-row (split to fit
+    shared memory) forms."""
+    import torch
+    vocab = 7
+    table = wl.numpy_quant_table(qtype, vocab, cols, seed=cols + offset)
+    buf = torch.zeros(table.size + 32, dtype=torch.uint8, device=cuda)
+    buf[offset:offset + table.size] = dev(table, cuda)
+    view = buf[offset:offset + table.size]
+    rng = np.random.default_rng(T + offset)
+    tokens = rng.integers(0, vocab, T).astype(np.int32)
+    tokens[:2] = [0, vocab - 1]
+    tokens[-1] = vocab - 1
+    want, bad = oracle.embedding(table, qtype, vocab, cols, tokens)
+    assert bad == 0
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = mlb.embedding_rows(view, qtype, vocab, cols, dev(tokens, cuda), status=status)
+    assert_bitexact(host(got), want, f"{wl.QNAME[qtype]} cols={cols} offset={offset}")
+    assert mlb.status_check(status) == 0
+
+
 # ---------------------------------------------------------------- configs
 
 @pytest.mark.parametrize("name", ["qwen2-0.5b-t256", "llama-7b-t64"])
