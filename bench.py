@@ -579,6 +579,81 @@ def config_block(cfg, args, tokens_per_gpu, global_tokens):
     }
 
 
+# ---------------------------------------------------------------- copy bound
+
+def copy_bandwidth(args):
+    """Pinned host <-> device copy bandwidth of the box, the bound of the
+    e2e number: every rank copies `COPY_BYTES` from pinned host memory on its
+    GPU's NUMA node to the device (h2d), back (d2h), and both at once on two
+    streams; times are device events, max over ranks after a common barrier.
+    Prints one JSON line with the aggregate GB/s over all ranks."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    n = COPY_BYTES
+    with pinned_near_gpu(local, True) as node:
+        h_in = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        h_out = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        h_in.fill_(1)
+    d_in = torch.empty(n, dtype=torch.uint8, device=dev)
+    d_out = torch.zeros(n, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(kind):
+        for _ in range(2):  # warm-up, then the timed pass
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            if kind in ("h2d", "both"):
+                ev[0].record(s_in)
+                with torch.cuda.stream(s_in):
+                    d_in.copy_(h_in, non_blocking=True)
+                ev[1].record(s_in)
+            if kind in ("d2h", "both"):
+                ev[2].record(s_out)
+                with torch.cuda.stream(s_out):
+                    h_out.copy_(d_out, non_blocking=True)
+                ev[3].record(s_out)
+            torch.cuda.synchronize()
+        ms = []
+        if kind in ("h2d", "both"):
+            ms.append(ev[0].elapsed_time(ev[1]))
+        if kind in ("d2h", "both"):
+            ms.append(ev[2].elapsed_time(ev[3]))
+        return max(ms)
+
+    res = torch.tensor([timed(k) for k in ("h2d", "d2h", "both")],
+                       dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(res, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    h2d_ms, d2h_ms, both_ms = res.cpu().tolist()
+    gb = n / 1e9
+    print(json.dumps({
+        "copy_bandwidth": True, "n_gpus": world, "bytes_per_gpu_per_direction": n,
+        "pinned_numa_node_rank0": node,
+        "h2d_gbs_aggregate": round(world * gb / (h2d_ms / 1e3), 1),
+        "d2h_gbs_aggregate": round(world * gb / (d2h_ms / 1e3), 1),
+        "both_directions_gbs_aggregate": round(2 * world * gb / (both_ms / 1e3), 1),
+        "h2d_gbs_per_gpu": round(gb / (h2d_ms / 1e3), 1),
+        "d2h_gbs_per_gpu": round(gb / (d2h_ms / 1e3), 1)}), flush=True)
+
+
+COPY_BYTES = 512 << 20
+
+
 # ---------------------------------------------------------------- main
 
 def gpu_arm(args, cfg):
@@ -868,9 +943,11 @@ def sweep(args):
     """Bandwidth sweep: every operator (RMSNorm, residual RMSNorm, SwiGLU,
     Q8_0 / Q4_0 / Q4_1 gather) x hidden size {512 .. 16384} x token count
     {1 .. 262144}, seed 1, quant tables of 32000 rows; one JSON line per point with
-    GB/s per GPU and the fractions of the measured and spec peaks.  Weak
-    scaling under torchrun: every rank runs the point on its own GPU and the
-    slowest rank's time is reported."""
+    GB/s per GPU and the fractions of the measured and spec peaks.  Under
+    torchrun a point's T rows are split into equal contiguous ranges, one per
+    rank (points whose T is not a multiple of the rank count are skipped),
+    and the slowest rank's time is reported; `--weak` runs the whole point on
+    every rank instead."""
     import torch
     import torch.distributed as dist
     import mlb
@@ -899,7 +976,10 @@ def sweep(args):
                 qt = {"emb_q8_0": wl.Q8_0, "emb_q4_0": wl.Q4_0,
                       "emb_q4_1": wl.Q4_1}[op]
                 table = wl.quant_table(qt, wl.SWEEP_VOCAB, H, dev, seed=1)
-            for T in tokens_list:
+            for T_point in tokens_list:
+                if world > 1 and not args.weak and T_point % world != 0:
+                    continue
+                T = T_point if (world == 1 or args.weak) else T_point // world
                 if op in ("rmsnorm", "res_rmsnorm"):
                     x = torch.randn((T, H), generator=g, **f32)
                     r = torch.randn((T, H), generator=g, **f32) \
@@ -926,8 +1006,10 @@ def sweep(args):
                 if rank == 0:
                     gbs = nbytes / (ms / 1e3) / 1e9
                     print(json.dumps({
-                        "sweep": op, "hidden": H, "tokens_per_gpu": T,
-                        "n_gpus": world, "ms": round(ms, 5),
+                        "sweep": op, "hidden": H, "tokens": T_point,
+                        "tokens_per_gpu": T, "n_gpus": world,
+                        "scaling": "weak" if args.weak else "strong",
+                        "ms": round(ms, 5),
                         "tokens_per_s": round(T * world / (ms / 1e3), 1),
                         "gbs_per_gpu": round(gbs, 1),
                         "frac_of_measured": round(gbs / peak, 4),
@@ -1040,6 +1122,8 @@ def main():
     ap.add_argument("--launch-overlap", type=int, default=1, choices=(0, 1),
                     help="1: programmatic dependent launch between kernels (the "
                          "library's default), 0: plain stream order")
+    ap.add_argument("--copy-bw", action="store_true",
+                    help="pinned host <-> device copy bandwidth (the e2e bound)")
     ap.add_argument("--sweep-ops", default="")
     ap.add_argument("--sweep-hidden", default="")
     ap.add_argument("--sweep-tokens", default="")
@@ -1048,6 +1132,9 @@ def main():
     if args.impl != "reference" and not args.prefill:
         import mlb
         mlb.set_launch_overlap(args.launch_overlap)
+    if args.copy_bw:
+        copy_bandwidth(args)
+        return
     if args.sweep:
         sweep(args)
         return

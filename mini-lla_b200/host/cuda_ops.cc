@@ -116,15 +116,95 @@ class RopeTables {
   std::map<std::tuple<int, uint32_t, int>, Entry> tables_;
 };
 
-// Uploads a host vector of int ids/positions into a pooled device buffer.
-DeviceBuffer UploadInts(const std::vector<int>& values) {
-  static_assert(sizeof(int) == sizeof(int32_t), "int must be 32-bit");
-  DeviceBuffer buffer;
-  if (values.empty()) return buffer;
-  buffer.Reset(values.size() * sizeof(int32_t));
-  buffer.Upload(values.data(), values.size() * sizeof(int32_t));
-  return buffer;
-}
+// Small host arrays (token ids, positions, softmax lengths) reach the device
+// without the host waiting for it: they are copied into a slot of pinned
+// memory and moved by cudaMemcpyAsync on the legacy default stream, ordered
+// before the kernel that reads them.  Every host thread has, per device, a
+// ring of kSlots slots; a slot is refilled once the copy that last read it
+// has completed (its event), so the host waits only when kSlots uploads are
+// still queued on the device.  Arrays above kSlotBytes take the blocking
+// DeviceBuffer::Upload.
+class IntStaging {
+ public:
+  static constexpr size_t kSlotBytes = size_t{256} << 10;  // 65536 ints
+  static constexpr int kSlots = 4;
+
+  static DeviceBuffer Upload(const std::vector<int>& values) {
+    static_assert(sizeof(int) == sizeof(int32_t), "int must be 32-bit");
+    DeviceBuffer buffer;
+    if (values.empty()) return buffer;
+    const size_t bytes = values.size() * sizeof(int32_t);
+    buffer.Reset(bytes);
+    if (bytes > kSlotBytes) {
+      buffer.Upload(values.data(), bytes);
+      return buffer;
+    }
+    thread_local IntStaging staging;
+    Ring& ring = staging.RingOf(CurrentDevice());
+    const int slot = ring.next;
+    ring.next = (ring.next + 1) % kSlots;
+    if (ring.used[slot]) {
+      const cudaError_t error = cudaEventSynchronize(ring.done[slot]);
+      if (error != cudaSuccess) Throw("int upload", error);
+    }
+    char* pinned = ring.pinned + static_cast<size_t>(slot) * kSlotBytes;
+    std::memcpy(pinned, values.data(), bytes);
+    cudaError_t error = cudaMemcpyAsync(buffer.data(), pinned, bytes, cudaMemcpyHostToDevice,
+                                        cudaStreamLegacy);
+    if (error == cudaSuccess) error = cudaEventRecord(ring.done[slot], cudaStreamLegacy);
+    if (error != cudaSuccess) Throw("int upload", error);
+    ring.used[slot] = true;
+    return buffer;
+  }
+
+  ~IntStaging() {
+    for (auto& entry : rings_) {
+      Ring& ring = entry.second;
+      for (int i = 0; i < kSlots; ++i) {
+        if (ring.used[i]) cudaEventSynchronize(ring.done[i]);
+        if (ring.done[i] != nullptr) cudaEventDestroy(ring.done[i]);
+      }
+      if (ring.pinned != nullptr) cudaFreeHost(ring.pinned);
+    }
+  }
+
+ private:
+  struct Ring {
+    char* pinned = nullptr;
+    cudaEvent_t done[kSlots] = {};
+    bool used[kSlots] = {};
+    int next = 0;
+  };
+
+  static int CurrentDevice() {
+    int device = 0;
+    const cudaError_t error = cudaGetDevice(&device);
+    if (error != cudaSuccess) Throw("cudaGetDevice", error);
+    return device;
+  }
+
+  [[noreturn]] static void Throw(const char* what, cudaError_t error) {
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(error));
+  }
+
+  // events belong to the device that was current when they were created
+  Ring& RingOf(int device) {
+    Ring& ring = rings_[device];
+    if (ring.pinned != nullptr) return ring;
+    cudaError_t error = cudaHostAlloc(reinterpret_cast<void**>(&ring.pinned),
+                                      kSlots * kSlotBytes, cudaHostAllocPortable);
+    if (error != cudaSuccess) Throw("cudaHostAlloc", error);
+    for (int i = 0; i < kSlots; ++i) {
+      error = cudaEventCreateWithFlags(&ring.done[i], cudaEventDisableTiming);
+      if (error != cudaSuccess) Throw("cudaEventCreate", error);
+    }
+    return ring;
+  }
+
+  std::map<int, Ring> rings_;
+};
+
+DeviceBuffer UploadInts(const std::vector<int>& values) { return IntStaging::Upload(values); }
 
 void RequireRope(float theta, int head_dim, const char* caller) {
   if (head_dim <= 0 || head_dim % 2 != 0) {

@@ -485,6 +485,78 @@ void TestShardingAndWaits(std::mt19937& rng) {
   cudaStreamDestroy(stream);
 }
 
+// The row-batched entries that take host arrays (token ids, scattered
+// positions, softmax lengths) queue their uploads instead of waiting for the
+// device: with the legacy stream held by a host function they return at
+// once, and their results are right once it is released.  Inputs, the pool
+// blocks and the RoPE table are made beforehand (a first round of the same
+// calls), since creating them copies synchronously.
+void TestNoHostWait(std::mt19937& rng) {
+  const int vocab = 64, cols = 512, rows = 300, nq = 4, nk = 2, hd = 64, width = 96;
+  const QuantizedTensor table = Quantize(Random({vocab, cols}, rng), QuantType::kQ4_1);
+  const CudaWeight dt = TableWeight(table);
+  std::vector<int> tokens(rows), positions(rows), lengths(rows);
+  for (int i = 0; i < rows; ++i) {
+    tokens[i] = (i * 13) % vocab;
+    positions[i] = (i * 7919) % 4096;
+    lengths[i] = i % width + 1;
+  }
+  const Tensor q = Random({rows, nq * hd}, rng), k = Random({rows, nk * hd}, rng);
+  const Tensor s = Random({rows, width}, rng, 2.0f);
+  const CudaTensor ds = CudaTensor::FromHost(s);
+  CudaTensor dq = CudaTensor::FromHost(q), dk = CudaTensor::FromHost(k);
+  auto round = [&](CudaTensor* emb, CudaTensor* soft) {
+    *emb = CudaEmbeddingRows(dt, tokens);
+    CudaRopeRows(&dq, &dk, nullptr, nullptr, positions, 1e4f, nq, nk, hd, RopeType::kNormal);
+    *soft = CudaSoftmaxRows(ds, &lengths);
+  };
+  {
+    CudaTensor e, p;
+    round(&e, &p);  // warm: pool blocks, RoPE table, pinned ring
+  }
+  CudaTensor qa = CudaTensor::FromHost(q), ka = CudaTensor::FromHost(k);
+  dq = std::move(qa);
+  dk = std::move(ka);
+  cudaDeviceSynchronize();
+  static std::atomic<bool> hold{false};
+  hold.store(true);
+  cudaLaunchHostFunc(cudaStreamLegacy, [](void*) {
+    for (int i = 0; i < 40000 && hold.load(); ++i) {
+      std::this_thread::sleep_for(std::chrono::microseconds(250));
+    }
+  }, nullptr);
+  const auto t0 = std::chrono::steady_clock::now();
+  CudaTensor emb, soft;
+  round(&emb, &soft);
+  const double ms = std::chrono::duration<double, std::milli>(
+                        std::chrono::steady_clock::now() - t0).count();
+  const bool held = cudaStreamQuery(cudaStreamLegacy) == cudaErrorNotReady;
+  hold.store(false);
+  Expect(held && ms < 2000.0,
+         "CudaEmbeddingRows / CudaRopeRows / CudaSoftmaxRows return without waiting (" +
+             std::to_string(ms) + " ms, stream held: " + (held ? "yes" : "no") + ")");
+  const Tensor ge = emb.Download(), gq = dq.Download(), gs = soft.Download();
+  bool ok = true;
+  std::vector<float> want(cols);
+  for (int i = 0; i < rows; ++i) {
+    DequantizeRow(table, tokens[i], want.data());
+    ok = ok && BitEqual(std::vector<float>(ge.data.begin() + i * cols,
+                                           ge.data.begin() + (i + 1) * cols), want);
+    Tensor qi({nq, hd}), ki({nk, hd});
+    std::copy(q.data.begin() + i * nq * hd, q.data.begin() + (i + 1) * nq * hd, qi.data.begin());
+    std::copy(k.data.begin() + i * nk * hd, k.data.begin() + (i + 1) * nk * hd, ki.data.begin());
+    Rope(qi, ki, positions[i], 1e4f, RopeType::kNormal);
+    ok = ok && BitEqual(std::vector<float>(gq.data.begin() + i * nq * hd,
+                                           gq.data.begin() + (i + 1) * nq * hd), qi.data);
+    Tensor vis({lengths[i]});
+    std::copy(s.data.begin() + i * width, s.data.begin() + i * width + lengths[i], vis.data.begin());
+    ok = ok && MaxRel(std::vector<float>(gs.data.begin() + i * width,
+                                         gs.data.begin() + i * width + lengths[i]),
+                      Softmax(vis).data) <= 1e-5;
+  }
+  Expect(ok, "queued uploads: gather bit-exact, RoPE bit-exact, softmax within 1e-5");
+}
+
 }  // namespace
 
 int main() {
@@ -495,6 +567,7 @@ int main() {
     TestEmbedding(rng);
     TestBatched(rng);
     TestShardingAndWaits(rng);
+    TestNoHostWait(rng);
     TestLinear(rng);
     TestAttention(rng);
     TestRuntime();

@@ -81,3 +81,37 @@ def test_prefill_driver_and_weight_upload_binary():
     res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "forward ok" in res.stdout
+
+
+def test_device_list_parsing_and_validation():
+    """oracle/_ref/mlb_devices_test --cpu: the multi-device backend's device
+    lists ("all", "0,2,3") and their validation with the reference's
+    exception types (backend.cc:26-42: invalid_argument for devices on a CPU
+    backend, out_of_range for an id outside the visible count; duplicates and
+    empty lists rejected), run against a given device count without a GPU."""
+    exe = os.path.join(REF, "mlb_devices_test")
+    if not os.path.exists(exe):
+        pytest.skip("mlb_devices_test not built (reference headers absent)")
+    res = subprocess.run([exe, "--cpu"], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "devices cpu ok" in res.stdout
+
+
+@pytest.mark.gpu
+def test_layer_ops_and_requests_split_across_devices():
+    """oracle/_ref/mlb_devices_test on two or more GPUs: weights replicated
+    from a host model and from the reference's GGUF fixture (every replica
+    byte-identical, on its own device); the layer-op chain over 1001 token
+    rows split across devices 0,1 and 1,0 bit-identical to one device, with
+    device 1's own RoPE table and pool; five requests spread over two devices
+    by ForwardBatchesCuda (prefill, then a decode step) bit-identical to one
+    device; a context moved to another device refused."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    exe = os.path.join(REF, "mlb_devices_test")
+    if not os.path.exists(exe):
+        pytest.skip("mlb_devices_test not built (reference headers absent)")
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "devices ok" in res.stdout
