@@ -550,9 +550,11 @@ def reference_arm(args, cfg):
         "value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": warm,
         "ms_per_step": round(res["sec_per_step"] * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": config_block(cfg, args, cfg.tokens),
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(cfg, args, cfg.tokens if args.weak else
+                               wl.shard_range(cfg.tokens, max(1, args.gpus), 0)[1],
+                               cfg.tokens * (max(1, args.gpus) if args.weak else 1)),
         "hbm_gbs_equiv": round(res["gbs"], 2),
         "cpu_baseline": {"value": round(res["tokens_per_s"], 1), "unit": "tokens/s",
                          "cores": res["cores"], "kind": res["kind"],
