@@ -273,8 +273,11 @@ int mlb_linear_rows_group_f32(int count, const void* const* w, int qtype,
  * Number of bounded device-side waits (a bulk weight copy that did not land
  * within the kernel's poll limit) that gave up on the current device since
  * the library was loaded.  A kernel that gives up leaves NaN in the outputs
- * it did not finish instead of hanging.  Synchronous.  Diagnostic only: no
- * counterpart in the reference.
+ * it did not finish instead of hanging.  Returns MLB_ERR_CUDA (with *count
+ * still set) when a waiting warp also gave up on copies it had in flight, so
+ * that a copy may have landed in shared memory after its block exited: the
+ * device's results since then are undefined.  Synchronous.  Diagnostic only:
+ * no counterpart in the reference.
  */
 int mlb_wait_timeouts(unsigned int* count);
 
@@ -349,8 +352,11 @@ int mlb_attention_rows_f32(const float* q, const float* keys,
  *   - Sizes whose mlb_attention_scratch_floats(...) exceeds 1 Mi floats are
  *     rejected with MLB_ERR_ARG and a message naming the need.
  *   - The first call on a device looks up the array's device address (once
- *     per device, with that device current); make that first call before any
- *     stream capture.
+ *     per device and context, with that device current) and keeps it; make
+ *     that first call before any stream capture.  A context created with
+ *     cuCtxCreate gets its own lookup.  Do not call it again on a device
+ *     after cudaDeviceReset of that device: the library's device code is
+ *     loaded anew there and the kept address may no longer be the array's.
  *   - Every call shares the one array and it keeps the last call's contents
  *     (nothing in it needs to start at zero): calls that overlap on the GPU —
  *     on different streams, or from several host threads — race.

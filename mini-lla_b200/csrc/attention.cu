@@ -912,32 +912,78 @@ namespace {
 constexpr int64_t kNoAllocScratchFloats = int64_t{1} << 20;  // 4 MiB
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-constexpr int kMaxNoAllocDevices = 64;
+// The array's device address differs per context (each context loads the
+// library's device code on its own), so the looked-up addresses are kept per
+// (context, device) — a caller that makes its own contexts (cuCtxCreate)
+// besides the primary one gets the address of each.  A cudaDeviceReset keeps
+// the primary context's handle but loads the code again, possibly elsewhere,
+// so an address kept from before a reset is not used again after it: the
+// entry point's contract asks callers not to reset a device they use it on.
+constexpr int kMaxNoAllocEntries = 64;
+struct NoAllocEntry {
+  void* context;
+  int device;
+  float* address;
+};
 std::mutex g_noalloc_mutex;
-float* g_noalloc_address[kMaxNoAllocDevices] = {};
+NoAllocEntry g_noalloc_entries[kMaxNoAllocEntries] = {};
+int g_noalloc_count = 0;
 
-// Device address of g_noalloc_scratch on the current device.  In host code
+// cuCtxGetCurrent through the runtime's driver entry point (no link against
+// the driver library); null when the driver does not offer it.
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn CtxGetCurrent() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Device address of g_noalloc_scratch in the current context.  In host code
 // the array's name only stands in for the symbol, so the address is looked up
-// once per device (with that device current) and cached.
+// with cudaGetSymbolAddress once per (context, device), with that device
+// current, and kept.
 int NoAllocScratch(float** out) {
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess)
     return Fail(MLB_ERR_CUDA, std::string("attention (no alloc): ") + cudaGetErrorString(err));
-  if (device < 0 || device >= kMaxNoAllocDevices)
-    return Fail(MLB_ERR_ARG, "attention (no alloc): device index beyond 63");
+  auto current = []() -> void* {  // null before any context is current
+    void* context = nullptr;
+    if (CtxGetCurrent() == nullptr || CtxGetCurrent()(&context) != 0) return nullptr;
+    return context;
+  };
+  void* context = current();
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_address[device] == nullptr) {
-    void* address = nullptr;
-    err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
-    if (err != cudaSuccess || address == nullptr) {
-      cudaGetLastError();
-      return Fail(MLB_ERR_CUDA, std::string("attention (no alloc): scratch address: ") +
-                                    cudaGetErrorString(err));
+  for (int i = 0; context != nullptr && i < g_noalloc_count; ++i) {
+    if (g_noalloc_entries[i].context == context && g_noalloc_entries[i].device == device) {
+      *out = g_noalloc_entries[i].address;
+      return MLB_OK;
     }
-    g_noalloc_address[device] = static_cast<float*>(address);
   }
-  *out = g_noalloc_address[device];
+  if (g_noalloc_count == kMaxNoAllocEntries)
+    return Fail(MLB_ERR_ARG, "attention (no alloc): more than 64 (context, device) pairs");
+  void* address = nullptr;
+  err = cudaGetSymbolAddress(&address, g_noalloc_scratch);  // makes a context current
+  if (err != cudaSuccess || address == nullptr) {
+    cudaGetLastError();
+    return Fail(MLB_ERR_CUDA, std::string("attention (no alloc): scratch address: ") +
+                                  cudaGetErrorString(err));
+  }
+  context = current();
+  bool known = false;
+  for (int i = 0; i < g_noalloc_count; ++i)
+    known = known || (g_noalloc_entries[i].context == context && g_noalloc_entries[i].device == device);
+  if (!known && context != nullptr)
+    g_noalloc_entries[g_noalloc_count++] = {context, device, static_cast<float*>(address)};
+  *out = static_cast<float*>(address);
   return MLB_OK;
 }
 

@@ -289,7 +289,11 @@ __device__ __forceinline__ bool BarTryWait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 // Bounded wait: gives up after kWaitLimit polls, ~2 s (a copy that never
-// lands must not hang the device).
+// lands must not hang the device).  A warp that gives up first waits, again
+// bounded, for its copies still in flight; if one of those waits gives up
+// too, the warp leaves with a copy pending into shared memory that its CTA
+// no longer owns once it exits, which g_wait_abandoned records (and
+// mlb_wait_timeouts reports as an error).
 constexpr int kWaitLimit = 1 << 21;
 __device__ __forceinline__ bool BarWait(uint64_t* bar, unsigned parity) {
   for (int i = 0; i < kWaitLimit; ++i)
@@ -307,9 +311,11 @@ __device__ __forceinline__ void BulkCopy(void* dst, const void* src, unsigned by
 
 }  // namespace
 
-// Waits that gave up (a bulk copy that did not land in time); read by
+// Waits that gave up (a bulk copy that did not land in time), and warps that
+// left with copies still pending after their bounded drain; read by
 // mlb_wait_timeouts.
 __device__ unsigned int g_wait_timeouts;
+__device__ unsigned int g_wait_abandoned;
 
 namespace {
 
@@ -486,7 +492,10 @@ __global__ void __launch_bounds__(kBulkMaxWarps * 32, 1)
       // leave NaN in the rows this warp did not finish
       if (lane == 0) atomicAdd(&g_wait_timeouts, 1u);
       const int last = s + kBulkStages - 1 < nseg ? s + kBulkStages - 1 : nseg - 1;
-      for (int r = s; r <= last; ++r) BarWait(bars + r % kBulkStages, (r / kBulkStages) & 1);
+      bool drained = true;
+      for (int r = s; r <= last; ++r)
+        drained = BarWait(bars + r % kBulkStages, (r / kBulkStages) & 1) && drained;
+      if (!drained && lane == 0) atomicAdd(&g_wait_abandoned, 1u);
       for (int64_t j = row; j < w1; ++j)
         if (lane < T) a.y[static_cast<int64_t>(lane) * a.n + j] = __int_as_float(0x7fc00000);
       return;
@@ -731,9 +740,16 @@ extern "C" int mlb_gemv_path(void) { return g_gemv_path; }
 extern "C" int mlb_wait_timeouts(unsigned int* count) {
   using namespace mlb;
   if (count == nullptr) return Fail(MLB_ERR_ARG, "mlb_wait_timeouts: null pointer");
-  if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess)
+  unsigned int abandoned = 0;
+  if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemcpyFromSymbol(&abandoned, g_wait_abandoned, sizeof(unsigned int)) != cudaSuccess)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
   *count += TcWaitTimeouts() + GemvTcWaitTimeouts() + LinearF16WaitTimeouts();
+  if (abandoned != 0)
+    return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: " + std::to_string(abandoned) +
+                                  " warp(s) gave up with bulk copies still pending into "
+                                  "shared memory; results on this device since then are "
+                                  "undefined");
   return MLB_OK;
 }
 

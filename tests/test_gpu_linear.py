@@ -107,6 +107,29 @@ def test_linear_rows_tensor_cores_vs_oracle(cuda, oracle, qtype, n, k, t):
     _check(got.cpu().numpy(), want, wdeq, x, f"rows {wl.QNAME[qtype]} n={n} k={k} t={t}")
 
 
+@pytest.mark.parametrize("qtype", [wl.Q8_0, wl.Q4_0])
+@pytest.mark.parametrize("k", [4160, 6144, 8192, 10240, 12288, 14336, 16384, 16448])
+def test_linear_rows_long_rows_vs_oracle(cuda, oracle, qtype, k):
+    """Rows long enough for every register width of the x split of the fp16
+    prompt path (one float4 per thread of 512 up to eight: k up to 16384,
+    k = 14336 being the Llama-3 down projection) and for its two-pass form
+    beyond (k = 16448); one row of x spans many binades, so the per-row
+    power-of-two scale and the second fp16 piece are exercised at these
+    lengths too."""
+    import torch
+    n, t = 64, 48
+    rng = np.random.default_rng(k + qtype)
+    table = wl.numpy_quant_table(qtype, n, k, seed=k)
+    x = rng.standard_normal((t, k), dtype=np.float32)
+    x[5] = (rng.standard_normal(k) * np.exp(rng.uniform(-10, 10, k))).astype(np.float32)
+    want = oracle.linear(table, qtype, n, k, x)
+    got = mlb.linear_rows(dev(table, cuda), qtype, n, k, dev(x, cuda))
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    wdeq, _ = oracle.embedding(table, qtype, n, k, np.arange(n, dtype=np.int32))
+    _check(got.cpu().numpy(), want, wdeq, x, f"long rows {wl.QNAME[qtype]} k={k}")
+
+
 def test_linear_rows_large_values_and_small_batches(cuda, oracle):
     """x spanning many binades (the tail split matters) and batches below the
     tensor-core threshold (the GEMV path) through the same entry."""
