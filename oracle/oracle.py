@@ -32,7 +32,10 @@ def build_oracle():
     """Compiles liboracle.so (and _ref/libmlref.so when the reference
     sources are reachable)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    ref_dir = os.environ.get("MLB_REFERENCE_DIR", "/root/reference")
+    # the reference checkout: MLB_REFERENCE_DIR, else `reference` beside
+    # this repository
+    ref_dir = os.environ.get("MLB_REFERENCE_DIR") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
     if os.path.isdir(os.path.join(ref_dir, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref",
                         f"MLB_REFERENCE_DIR={ref_dir}"], check=True)
