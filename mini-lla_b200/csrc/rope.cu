@@ -134,7 +134,8 @@ __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
 // the layer-op step (after the residual RMSNorm), MAXI = 1 / 3 took 0.117 /
 // 0.123 ms against 0.118 for the item loop above — more loads in flight
 // compete with the write-back of the previous kernel's dirty L2 lines — and
-// 0.108 / 0.107 / 0.109 ms alone.
+// 0.108 / 0.107 / 0.109 ms alone (256-thread CTAs; see the launch for the
+// CTA size).
 template <bool NEOX, int MAXI>
 __global__ void __launch_bounds__(256) RopeRowsKernel(RopeArgs a, int G) {
   LaunchWait();  // the previous kernel on the stream has completed
@@ -284,8 +285,12 @@ extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
       if (neox) Launch(RopeVecKernel<true, true>, grid2, threads, 0, s, a);
       else Launch(RopeVecKernel<false, true>, grid2, threads, 0, s, a);
     } else if (G <= 256) {
-      // heads per pass: as many as fit 256 threads, no more than there are
-      int hpp = 256 / G;
+      // heads per pass: as many as fit 128 threads (at least one), no more
+      // than there are.  Measured on B200 in the layer-op step: 128-thread
+      // CTAs beat 256 (40 heads x 128 normal, 16384 tokens: 0.114 against
+      // 0.116 ms; 28 + 4 heads x 128 NeoX with bias, 65536 tokens: 0.339
+      // against 0.405 ms; the item loop above 0.117 / 0.360 ms at 256)
+      int hpp = G <= 128 ? 128 / G : 1;
       if (hpp > nq + nk) hpp = nq + nk;
       const int rthreads = hpp * G;
       if (neox) Launch(RopeRowsKernel<true, 1>, grid, rthreads, 0, s, a, G);
