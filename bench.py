@@ -390,8 +390,16 @@ def graph_timing(step: LayerStep, args, world, cold: bool):
         return g
 
     step_graph = capture(step.step)
-    op_graphs = [capture(lambda op=op: step.launch(op)) for op in step.ops]
-    if cold and _flush_buf is None:
+    # an operator whose own bytes are under 2 x L2 is timed cold as well (a
+    # graph of one launch after an L2 eviction), whatever the step's size
+    op_bytes = step.bytes()
+    op_cold = [cold or op_bytes[op] < 2 * L2_BYTES for op in step.ops]
+    op_graphs = []
+    for op, oc in zip(step.ops, op_cold):
+        saved, repeat = repeat, (1 if oc else repeat)
+        op_graphs.append(capture(lambda op=op: step.launch(op)))
+        repeat = saved
+    if any(op_cold) and _flush_buf is None:
         _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
     replays = max(1, args.steps // repeat)
     for g in [step_graph] + op_graphs:
@@ -437,7 +445,10 @@ def graph_timing(step: LayerStep, args, world, cold: bool):
             dist.barrier()
     total_ms = start.elapsed_time(end) * args.steps / (replays * repeat)
     op_ms = []
-    for g in op_graphs:
+    for g, oc in zip(op_graphs, op_cold):
+        if oc:
+            op_ms.append(statistics.median(cold_times(g, min(args.steps, 21))))
+            continue
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record()
@@ -724,7 +735,10 @@ def gpu_arm(args, cfg):
     step = LayerStep(cfg, dev, tokens, pos_offset, ops)
     nops = len(step.ops)
     op_bytes = step.bytes()
-    use_graph = args.graph == "on" or (args.graph == "auto" and tokens <= 2048)
+    # CUDA-graph replay where the host could not enqueue a step's launches
+    # faster than the GPU runs them (measured: 4096 rows per GPU over 4 ranks
+    # spent a quarter of each step waiting on the host with direct launches)
+    use_graph = args.graph == "on" or (args.graph == "auto" and (tokens <= 4096 or world > 1))
     # a working set under 2 x L2 would be read from L2 by back-to-back steps:
     # such steps are timed one at a time after an L2 eviction
     cold = sum(op_bytes.values()) < 2 * L2_BYTES
@@ -949,6 +963,46 @@ def attention_bench(args):
             "timing": "cold L2" if nbytes < 2 * L2_BYTES else "warm"}), flush=True)
         del keys, values
         torch.cuda.empty_cache()
+    attention_rows_bench(args)
+
+
+ATTENTION_ROWS_CASES = (  # (name, n_heads, n_kv_heads, head_dim, position, rows)
+    ("llama3-8b", 32, 8, 128, 0, 512), ("llama3-8b", 32, 8, 128, 0, 2048),
+    ("llama3-8b", 32, 8, 128, 2048, 2048), ("qwen2-7b", 28, 4, 128, 0, 2048),
+    ("qwen2-0.5b", 14, 2, 64, 0, 2048))
+
+
+def attention_rows_bench(args):
+    """Causal attention of a prompt chunk (mlb_attention_rows_f32) on the
+    CUDA-core kernels and on the tensor cores: one JSON line per (case,
+    path), TFLOP/s over the fp32-equivalent flops of the causal products
+    (2 x 2 x hd per visible (query head, key) pair)."""
+    import torch
+    import mlb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    for name, nh, nkv, hd, pos, rows in ATTENTION_ROWS_CASES:
+        max_seq = pos + rows
+        keys = torch.randn((max_seq, nkv, hd), generator=g, device=dev)
+        values = torch.randn((max_seq, nkv, hd), generator=g, device=dev)
+        q = torch.randn((rows, nh, hd), generator=g, device=dev)
+        out = torch.empty((rows, nh, hd), device=dev)
+        pairs = nh * (rows * pos + rows * (rows + 1) // 2)
+        flops = 4.0 * hd * pairs
+        for path in (1, 2):
+            previous = mlb.set_attention_path(path)
+            fn = lambda: mlb.attention_rows(q, keys, values, pos, out=out)  # noqa: E731
+            ms = time_fn(fn, 1 << 40, 1)  # compute-bound: back-to-back launches
+            mlb.set_attention_path(previous)
+            print(json.dumps({
+                "attention_rows": name, "heads": nh, "kv_heads": nkv, "head_dim": hd,
+                "position": pos, "rows": rows,
+                "path": "tensor cores (TF32 head + tail)" if path == 2 else "CUDA cores",
+                "ms": round(ms, 4), "tflops_fp32_equiv": round(flops / (ms / 1e3) / 1e12, 1)}),
+                flush=True)
+        del keys, values, q, out
+        torch.cuda.empty_cache()
 
 
 # ---------------------------------------------------------------- prefill
@@ -1147,7 +1201,8 @@ def main():
     ap.add_argument("--ops", default="",
                     help="comma list: time only these operators of the step")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
-                    help="replay the step from a CUDA graph (auto: T <= 2048)")
+                    help="replay the step from a CUDA graph (auto: T <= 4096 rows per "
+                         "GPU, or several GPUs)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="token rows per step instead of the workload's T")
     ap.add_argument("--sweep", action="store_true",
