@@ -342,6 +342,19 @@ int mlb_attention_rows_f32(const float* q, const float* keys,
                            int64_t scratch_floats, void* stream);
 
 /*
+ * Kernel choice of mlb_attention_rows_f32 for prompt chunks (two rows or
+ * more): 0 = automatic (the default: the tensor cores from 1024 rows),
+ * 1 = always the CUDA-core
+ * kernels, 2 = the tensor cores wherever the shape allows (group 1 .. 8,
+ * head_dim 64 or 128, 16-byte aligned tensors).  Process-wide; for benchmarks
+ * and tests.  Returns MLB_OK, or MLB_ERR_ARG for another value;
+ * mlb_attention_path returns the current setting.  No counterpart in the
+ * reference.
+ */
+int mlb_set_attention_path(int path);
+int mlb_attention_path(void);
+
+/*
  * Decode attention that allocates nothing.  No counterpart in the reference:
  * it is mlb_attention_decode_f32 for callers that cannot provide device
  * scratch — a plugin inside a host framework that owns every device

@@ -685,6 +685,7 @@ int GemvTc(int qtype, int count, const void* const* w, const int64_t* n, int64_t
            const float* x, int tokens, float* const* y, int split, cudaStream_t s);
 unsigned int GemvTcWaitTimeouts();
 unsigned int LinearF16WaitTimeouts();  // linear_f16.cu
+unsigned int AttnTcWaitTimeouts();     // attention_tc.cu
 }  // namespace mlb
 
 namespace {
@@ -744,7 +745,8 @@ extern "C" int mlb_wait_timeouts(unsigned int* count) {
   if (cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(unsigned int)) != cudaSuccess ||
       cudaMemcpyFromSymbol(&abandoned, g_wait_abandoned, sizeof(unsigned int)) != cudaSuccess)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: read failed");
-  *count += TcWaitTimeouts() + GemvTcWaitTimeouts() + LinearF16WaitTimeouts();
+  *count += TcWaitTimeouts() + GemvTcWaitTimeouts() + LinearF16WaitTimeouts() +
+            AttnTcWaitTimeouts();
   if (abandoned != 0)
     return Fail(MLB_ERR_CUDA, "mlb_wait_timeouts: " + std::to_string(abandoned) +
                                   " warp(s) gave up with bulk copies still pending into "

@@ -52,6 +52,8 @@ SIGNATURES = {
     "mlb_status_check": (c_int, [c_void_p, c_void_p, c_void_p]),
     "mlb_wait_timeouts": (c_int, [c_void_p]),
     "mlb_set_gemv_path": (c_int, [c_int]),
+    "mlb_set_attention_path": (c_int, [c_int]),
+    "mlb_attention_path": (c_int, []),
     "mlb_gemv_path": (c_int, []),
     "mlb_set_launch_overlap": (c_int, [c_int]),
     "mlb_launch_overlap": (c_int, []),
@@ -478,6 +480,15 @@ def set_gemv_path(path: int) -> int:
     the previous setting."""
     previous = load().mlb_gemv_path()
     _check(load().mlb_set_gemv_path(int(path)), "set_gemv_path")
+    return previous
+
+
+def set_attention_path(path: int) -> int:
+    """Kernel choice of attention_rows() for prompt chunks: 0 automatic, 1
+    CUDA-core kernels, 2 tensor cores wherever the shape allows.  Returns the
+    previous setting."""
+    previous = load().mlb_attention_path()
+    _check(load().mlb_set_attention_path(int(path)), "set_attention_path")
     return previous
 
 

@@ -102,13 +102,25 @@ def test_kv_write_is_a_copy(cuda):
         mlb.kv_write(keys, values, dev(kb, cuda), dev(vb, cuda), 46)
 
 
+@pytest.fixture
+def attention_path():
+    """Sets mlb_set_attention_path for one test and restores it after."""
+    previous = mlb.set_attention_path(0)
+    yield mlb.set_attention_path
+    mlb.set_attention_path(previous)
+
+
+@pytest.mark.parametrize("path", [0, 1])
 @pytest.mark.parametrize("nh,nkv,hd,pos,rows,max_seq", [
     (4, 2, 8, 0, 1, 16), (8, 2, 64, 0, 37, 64), (32, 8, 128, 100, 64, 512),
     (14, 2, 64, 0, 256, 256), (28, 4, 128, 2000, 48, 4096), (8, 8, 32, 5, 300, 400)])
-def test_attention_rows_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max_seq):
+def test_attention_rows_vs_oracle(cuda, oracle, attention_path, path, nh, nkv, hd, pos, rows,
+                                  max_seq):
     """Row r of a prompt chunk equals decode attention at position pos + r
-    (the reference's per-token loop, batch.cc:26-41 over forward.cc:50-95)."""
+    (the reference's per-token loop, batch.cc:26-41 over forward.cc:50-95),
+    with the automatic kernel choice and with the CUDA-core kernels."""
     import torch
+    attention_path(path)
     rng = np.random.default_rng(nh * 7 + rows)
     q = rng.standard_normal((rows, nh, hd), dtype=np.float32)
     keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
@@ -146,11 +158,16 @@ def torch_zeros(shape, device):
     (32, 8, 64, 33, 333, 400),      # head_dim 64, ragged everything
     (28, 4, 128, 0, 700, 800),      # group 7 (Qwen2-7B): 9 rows = 63 vectors per tile
     (24, 8, 64, 10, 400, 500)])     # group 3: 21 rows = 63 vectors
-def test_attention_row_tiles_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max_seq):
-    """Prompt chunks large enough for the query-row tile kernel (n_kv_heads x
-    row tiles >= half the SMs): sampled rows (first, last, tile edges, random)
-    against per-position decode attention of the oracle."""
+@pytest.mark.parametrize("path", [1, 2])
+def test_attention_row_tiles_vs_oracle(cuda, oracle, attention_path, path, nh, nkv, hd, pos,
+                                       rows, max_seq):
+    """Prompt chunks large enough for the query-row tile kernels — the CUDA-core
+    one (path 1; n_kv_heads x row tiles >= half the SMs) and the tensor-core
+    one (path 2; 128 query vectors per tile, TF32 head + tail splits of Q, K,
+    P and V): sampled rows (first, last, tile edges, random) against
+    per-position decode attention of the oracle."""
     import torch
+    attention_path(path)
     rng = np.random.default_rng(rows + pos)
     q = rng.standard_normal((rows, nh, hd), dtype=np.float32)
     keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
@@ -158,7 +175,7 @@ def test_attention_row_tiles_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max
     got = mlb.attention_rows(dev(q, cuda), dev(keys, cuda), dev(values, cuda), pos)
     torch.cuda.synchronize()
     got = got.cpu().numpy()
-    qr = 64 // (nh // nkv)
+    qr = (64 if path == 1 else 128) // (nh // nkv)
     sample = {0, 1, rows - 1, rows - 2, qr - 1, qr, min(rows - 1, 2 * qr + 1)}
     sample |= set(rng.integers(0, rows, 6).tolist())
     for r in sorted(sample):
@@ -167,3 +184,67 @@ def test_attention_row_tiles_vs_oracle(cuda, oracle, nh, nkv, hd, pos, rows, max
         err = np.abs(got[r].astype(np.float64) - want)
         ratio = float((err / np.maximum(mag, 1e-30)).max())
         assert ratio <= 1e-5, f"row {r}: max error / magnitude {ratio:.2e}"
+
+
+def _exact_attention(q, keys, values, position, n_heads, n_kv):
+    """Decode attention of one row in float64 (the ground truth the fp32
+    reference itself only approximates)."""
+    hd = q.shape[1]
+    group = n_heads // n_kv
+    out = np.empty((n_heads, hd))
+    for h in range(n_heads):
+        k = keys[:position + 1, h // group].astype(np.float64)
+        v = values[:position + 1, h // group].astype(np.float64)
+        s = (k @ q[h].astype(np.float64)) * (1.0 / np.sqrt(np.float64(hd)))
+        w = np.exp(s - s.max())
+        out[h] = (w / w.sum()) @ v
+    return out
+
+
+@pytest.mark.parametrize("nh,nkv,hd,pos,rows,max_seq,spread", [
+    (32, 8, 128, 0, 2, 64, 1.0),      # two rows: one tile of mostly padding
+    (8, 8, 64, 3, 5, 40, 1.0),        # group 1, head_dim 64, a few rows
+    (32, 8, 128, 0, 300, 400, 6.0),   # wide score spread: the reference max moves, O rescaled
+    (16, 2, 128, 50, 200, 300, 12.0), # group 8, very peaked softmax
+    (28, 4, 128, 0, 129, 160, 3.0)])  # group 7 tiles of 18 rows, one row past a tile
+def test_attention_rows_tensor_cores_edges(cuda, oracle, attention_path, nh, nkv, hd, pos,
+                                           rows, max_seq, spread):
+    """The tensor-core prompt kernel on its edges: tiles that are mostly
+    padding, head_dim 64, and scores spread widely enough that the softmax's
+    reference max moves by more than 8 mid-row (O rescaled in tensor
+    memory); every row checked, keys past the last written position left as
+    garbage (NaN) to prove they are never read.
+
+    Bar: 1e-5 * sum_t w_t |v_t[i]| as everywhere.  With scores of standard
+    deviation 6 or 12 the reference's own fp32 dot products are off by more
+    than that (their rounding grows with sum_i |q_i k_i|), so there the
+    worst error over all rows, relative to that magnitude, must stay within
+    the larger of 1e-5 and twice the reference's own worst error over the
+    same rows, both measured against a float64 evaluation (row by row, two
+    roundings of this size are noise against noise)."""
+    import torch
+    attention_path(2)
+    rng = np.random.default_rng(rows * 3 + hd)
+    q = (rng.standard_normal((rows, nh, hd)) * spread).astype(np.float32)
+    keys = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    keys[:, :, :4] *= np.linspace(0.1, 3.0, max_seq, dtype=np.float32)[:, None, None]
+    values = rng.standard_normal((max_seq, nkv, hd), dtype=np.float32)
+    keys[pos + rows:] = np.nan
+    values[pos + rows:] = np.nan
+    got = mlb.attention_rows(dev(q, cuda), dev(keys, cuda), dev(values, cuda), pos)
+    torch.cuda.synchronize()
+    assert mlb.wait_timeouts() == 0
+    got = got.cpu().numpy()
+    ours = theirs = 0.0
+    for r in range(rows):
+        want = oracle.attention_decode(q[r], keys, values, pos + r, nh, nkv)
+        mag = np.maximum(_magnitude(q[r], keys, values, pos + r, nh, nkv), 1e-30)
+        if spread > 3.0:
+            exact = _exact_attention(q[r], keys, values, pos + r, nh, nkv)
+            ours = max(ours, float((np.abs(got[r].astype(np.float64) - exact) / mag).max()))
+            theirs = max(theirs, float((np.abs(want - exact) / mag).max()))
+        else:
+            ratio = float((np.abs(got[r].astype(np.float64) - want) / mag).max())
+            assert ratio <= 1e-5, f"row {r}: max error / magnitude {ratio:.2e}"
+    assert ours <= max(1e-5, 2.0 * theirs), \
+        f"worst error {ours:.2e}, the reference's own {theirs:.2e}"
