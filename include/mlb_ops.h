@@ -343,7 +343,7 @@ int mlb_attention_rows_f32(const float* q, const float* keys,
 
 /*
  * Kernel choice of mlb_attention_rows_f32 for prompt chunks (two rows or
- * more): 0 = automatic (the default: the tensor cores from 1024 rows),
+ * more): 0 = automatic (the default: the tensor cores from 512 rows),
  * 1 = always the CUDA-core
  * kernels, 2 = the tensor cores wherever the shape allows (group 1 .. 8,
  * head_dim 64 or 128, 16-byte aligned tensors).  Process-wide; for benchmarks

@@ -788,11 +788,11 @@ int AttentionRows(const float* q, const float* keys, const float* values, float*
   if (rows < 1 || position + rows > max_seq)
     return Fail(MLB_ERR_RANGE, "attention: rows leave the cache");
   cudaStream_t s = AsStream(stream);
-  // the tensor cores from 1024 query rows (automatic: measured on B200 at
-  // 32 / 8 heads x 128, 2048 rows 0.73 ms against 1.10 on the CUDA cores, 512
-  // rows 0.107 against 0.088), or for any prompt chunk of two rows or more
-  // (path 2)
-  if (rows > 1 && g_attention_path != 1 && (g_attention_path == 2 || rows >= 1024)) {
+  // the tensor cores from 512 query rows (automatic: measured on B200 at
+  // 32 / 8 heads x 128, 2048 rows 0.52 ms against 1.09 on the CUDA cores, 512
+  // rows 0.083 against 0.086, fewer rows slower), or for any prompt chunk of
+  // two rows or more (path 2)
+  if (rows > 1 && g_attention_path != 1 && (g_attention_path == 2 || rows >= 512)) {
     rc = AttentionRowsTc(q, keys, values, out, position, rows, n_heads, n_kv_heads, hd, s);
     if (rc >= 0) return rc;  // -1: shape not covered
   }

@@ -357,7 +357,33 @@ __global__ void __launch_bounds__(kAtThreads, 1) AttnTcKernel(const AtArgs a) {
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ loaders
+    // Block b + 1's rows are loaded into registers as soon as block b's
+    // pieces are stored, so their latency passes while the loader waits for
+    // the next stage to be free; all of a block's loads are in flight at
+    // once.  K: lane = float4 chunk along hd, keys lw, lw + 4, ...; V: lane =
+    // key, float4 chunks lw, lw + 4, ... of hd (stored transposed).
+    constexpr int KR = kAtKeys / 4;  // keys per loader warp
+    constexpr int VC = HD / 16;      // V float4 chunks per lane
     const int lw = warp - 4;
+    float4 kx[KR], vx[VC];
+    auto load_block = [&](int b) {
+#pragma unroll
+      for (int i = 0; i < KR; ++i) {
+        const int64_t t = static_cast<int64_t>(b) * kAtKeys + lw + 4 * i;
+        kx[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane < HD / 4 && t < kv_limit)
+          kx[i] = *reinterpret_cast<const float4*>(a.keys + t * kv_stride +
+                                                   static_cast<int64_t>(g) * HD + 4 * lane);
+      }
+      const int64_t t = static_cast<int64_t>(b) * kAtKeys + lane;
+      const float* vrow = a.values + t * kv_stride + static_cast<int64_t>(g) * HD;
+#pragma unroll
+      for (int i = 0; i < VC; ++i) {
+        vx[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < kv_limit) vx[i] = *reinterpret_cast<const float4*>(vrow + 4 * (lw + 4 * i));
+      }
+    };
+    if (nb > 0) load_block(0);
     for (int b = 0; b < nb; ++b) {
       const int s = b & 1;
       if (b >= 2 && !warp_wait(pv_done(s), ((b - 2) >> 1) & 1)) {
@@ -369,38 +395,28 @@ __global__ void __launch_bounds__(kAtThreads, 1) AttnTcKernel(const AtArgs a) {
       uint8_t* klp = base + (kl(s) - sbase);
       uint8_t* vhp = base + (vh(s) - sbase);
       uint8_t* vlp = base + (vl(s) - sbase);
-      // K: lane = float4 chunk along hd, rows key = lw, lw + 4, ...
       if (lane < HD / 4) {
         const int st = lane >> 3, ch = lane & 7;
-#pragma unroll 2
-        for (int key = lw; key < kAtKeys; key += 4) {
-          const int64_t t = static_cast<int64_t>(b) * kAtKeys + key;
-          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (t < kv_limit)
-            x = *reinterpret_cast<const float4*>(a.keys + t * kv_stride +
-                                                 static_cast<int64_t>(g) * HD + 4 * lane);
+#pragma unroll
+        for (int i = 0; i < KR; ++i) {
+          const int key = lw + 4 * i;
           float4 h, mid, r;
-          Tf32Split3(x.x, h.x, mid.x, r.x);
-          Tf32Split3(x.y, h.y, mid.y, r.y);
-          Tf32Split3(x.z, h.z, mid.z, r.z);
-          Tf32Split3(x.w, h.w, mid.w, r.w);
+          Tf32Split3(kx[i].x, h.x, mid.x, r.x);
+          Tf32Split3(kx[i].y, h.y, mid.y, r.y);
+          Tf32Split3(kx[i].z, h.z, mid.z, r.z);
+          Tf32Split3(kx[i].w, h.w, mid.w, r.w);
           const uint32_t off = static_cast<uint32_t>(st * (kAtKeys * 128)) + AtSwz(key, ch);
           *reinterpret_cast<float4*>(khp + off) = h;
           *reinterpret_cast<float4*>(kmp + off) = mid;
           *reinterpret_cast<float4*>(klp + off) = r;
         }
       }
-      // V transposed: lane = key, float4 chunks c4 = lw, lw + 4, ... of hd
       {
-        const int64_t t = static_cast<int64_t>(b) * kAtKeys + lane;
-        const bool valid = t < kv_limit;
-        const float* vrow = a.values + t * kv_stride + static_cast<int64_t>(g) * HD;
         const int ch = lane >> 2, w = lane & 3;
-#pragma unroll 2
-        for (int c4 = lw; c4 < HD / 4; c4 += 4) {
-          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (valid) x = *reinterpret_cast<const float4*>(vrow + 4 * c4);
-          const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int i = 0; i < VC; ++i) {
+          const int c4 = lw + 4 * i;
+          const float xs[4] = {vx[i].x, vx[i].y, vx[i].z, vx[i].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int d = 4 * c4 + e;
@@ -414,6 +430,7 @@ __global__ void __launch_bounds__(kAtThreads, 1) AttnTcKernel(const AtArgs a) {
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       AtArrive(kv_full(s));
+      if (b + 1 < nb) load_block(b + 1);
     }
   } else {
     // ------------------------------------------------------------ softmax
