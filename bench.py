@@ -362,22 +362,76 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8, numa: bool = True):
 GRAPH_REPEAT = 10
 
 
-def graph_timing(step: LayerStep, args, world, cold: bool):
-    """Latency-bound batches: the step's launches are captured once in a CUDA
-    graph and replayed.  With `cold` (the step's working set is under 2 x
-    L2, so back-to-back steps would read it from L2) every step runs alone
-    after an L2 eviction — a read of a 512 MiB buffer and a ~0.5 ms device
-    sleep, both outside the events — and the median step is kept; otherwise
-    GRAPH_REPEAT steps per graph are replayed back to back.  Per-operator
-    times come from graphs of that operator alone, timed the same way.
-    Returns total ms over args.steps steps, per-op ms, and the clock
-    sampler."""
+def cold_timing(step: LayerStep, args, world):
+    """Steps whose working set is under 2 x L2 (back-to-back steps would
+    read it from L2): every step runs alone after an L2 eviction — a read of
+    a 512 MiB buffer, then a ~0.5 ms device sleep during which the host
+    enqueues the step's launches and events — so the events bracket only the
+    step's kernels; the median step and the median of each operator's events
+    inside it are kept.  Returns total ms over args.steps steps, per-op ms,
+    and the clock sampler."""
     import torch
     import torch.distributed as dist
     global _flush_buf
+    if _flush_buf is None:
+        _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
+    nops = len(step.ops)
+    totals, per_op = [], [[] for _ in range(nops)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        for _ in range(args.steps):
+            events = [torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
+            _flush_buf.sum()  # evicts L2, leaving only clean lines
+            torch.cuda._sleep(1_000_000)  # the host enqueues the step meanwhile
+            step.step(events)
+            torch.cuda.synchronize()
+            totals.append(events[0].elapsed_time(events[nops]))
+            for j in range(nops):
+                per_op[j].append(events[j].elapsed_time(events[j + 1]))
+        if world > 1:
+            dist.barrier()
+    return (statistics.median(totals) * args.steps,
+            [statistics.median(t) for t in per_op], sampler)
+
+
+def cold_op_ms(step: LayerStep, op: str, count: int) -> float:
+    """Median device time of one launch of `op` alone after an L2 eviction
+    (a 512 MiB read, then a ~0.5 ms device sleep during which the host
+    enqueues the launch)."""
+    import torch
+    global _flush_buf
+    if _flush_buf is None:
+        _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
+    times = []
+    for _ in range(count):
+        _flush_buf.sum()
+        torch.cuda._sleep(1_000_000)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step.launch(op)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def graph_timing(step: LayerStep, args, world):
+    """Steps whose launches the host could not enqueue as fast as the GPU runs
+    them: GRAPH_REPEAT steps are captured in one CUDA graph and replayed back
+    to back (the step's working set is at least 2 x L2, so no step reads the
+    previous one's data from L2).  Per-operator times: an operator whose own
+    bytes reach 2 x L2 from a graph of GRAPH_REPEAT launches of it alone,
+    replayed back to back; a smaller one as the median of single launches
+    after an L2 eviction.  Returns total ms over args.steps steps, per-op ms,
+    and the clock sampler."""
+    import torch
+    import torch.distributed as dist
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
-    repeat = 1 if cold else GRAPH_REPEAT
 
     def capture(fn):
         g = torch.cuda.CUDAGraph()
@@ -385,56 +439,24 @@ def graph_timing(step: LayerStep, args, world, cold: bool):
             fn()  # warm the capture stream once outside the graph
             torch.cuda.synchronize()
             with torch.cuda.graph(g, stream=stream):
-                for _ in range(repeat):
+                for _ in range(GRAPH_REPEAT):
                     fn()
         return g
 
     step_graph = capture(step.step)
-    # an operator whose own bytes are under 2 x L2 is timed cold as well (a
-    # graph of one launch after an L2 eviction), whatever the step's size
     op_bytes = step.bytes()
-    op_cold = [cold or op_bytes[op] < 2 * L2_BYTES for op in step.ops]
-    op_graphs = []
-    for op, oc in zip(step.ops, op_cold):
-        saved, repeat = repeat, (1 if oc else repeat)
-        op_graphs.append(capture(lambda op=op: step.launch(op)))
-        repeat = saved
-    if any(op_cold) and _flush_buf is None:
-        _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
-    replays = max(1, args.steps // repeat)
-    for g in [step_graph] + op_graphs:
+    op_graphs = {op: capture(lambda op=op: step.launch(op)) for op in step.ops
+                 if op_bytes[op] >= 2 * L2_BYTES}
+    replays = max(1, args.steps // GRAPH_REPEAT)
+    for g in [step_graph] + list(op_graphs.values()):
         g.replay()
     torch.cuda.synchronize()
-
-    def cold_times(graph, count):
-        times = []
-        for _ in range(count):
-            _flush_buf.sum()  # evicts L2, leaving only clean lines
-            torch.cuda._sleep(1_000_000)  # the host enqueues the replay meanwhile
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            graph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            times.append(e0.elapsed_time(e1))
-        return times
-
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(torch.cuda.current_device())
-    if cold:
-        with sampler:
-            times = cold_times(step_graph, args.steps)
-            if world > 1:
-                dist.barrier()
-        total_ms = statistics.median(times) * args.steps
-        op_ms = [statistics.median(cold_times(g, min(args.steps, 21))) for g in op_graphs]
-        del step_graph, op_graphs
-        return total_ms, op_ms, sampler
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device())
     with sampler:
         start.record()
         for _ in range(replays):
@@ -443,20 +465,20 @@ def graph_timing(step: LayerStep, args, world, cold: bool):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    total_ms = start.elapsed_time(end) * args.steps / (replays * repeat)
+    total_ms = start.elapsed_time(end) * args.steps / (replays * GRAPH_REPEAT)
     op_ms = []
-    for g, oc in zip(op_graphs, op_cold):
-        if oc:
-            op_ms.append(statistics.median(cold_times(g, min(args.steps, 21))))
+    for op in step.ops:
+        if op not in op_graphs:
+            op_ms.append(cold_op_ms(step, op, min(args.steps, 21)))
             continue
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record()
         for _ in range(replays):
-            g.replay()
+            op_graphs[op].replay()
         s1.record()
         torch.cuda.synchronize()
-        op_ms.append(s0.elapsed_time(s1) / (replays * repeat))
+        op_ms.append(s0.elapsed_time(s1) / (replays * GRAPH_REPEAT))
     del step_graph, op_graphs
     return total_ms, op_ms, sampler
 
@@ -742,13 +764,13 @@ def gpu_arm(args, cfg):
     # a working set under 2 x L2 would be read from L2 by back-to-back steps:
     # such steps are timed one at a time after an L2 eviction
     cold = sum(op_bytes.values()) < 2 * L2_BYTES
-    if cold:
-        use_graph = True
     for _ in range(args.warmup):
         step.step()
     torch.cuda.synchronize()
-    if use_graph:
-        total_ms, op_ms, sampler = graph_timing(step, args, world, cold)
+    if cold:
+        total_ms, op_ms, sampler = cold_timing(step, args, world)
+    elif use_graph:
+        total_ms, op_ms, sampler = graph_timing(step, args, world)
     else:
         events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
                   for _ in range(args.steps)]
@@ -830,7 +852,7 @@ def gpu_arm(args, cfg):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3),
             "pinned_numa_node": getattr(step, "e2e_numa_node", None)},
-        "timing": ("cuda graph replay, one step at a time after an L2 eviction" if cold
+        "timing": ("direct launches, one step at a time after an L2 eviction" if cold
                    else "cuda graph replay" if use_graph else "direct launches"),
         "launch_overlap": args.launch_overlap,
         "gpu_launches": args.steps * len(step.ops),
@@ -982,7 +1004,10 @@ def attention_rows_bench(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(2)
-    for name, nh, nkv, hd, pos, rows in ATTENTION_ROWS_CASES:
+    cases = ATTENTION_ROWS_CASES
+    if args.attention_rows:  # one Llama-3-8B case of that many rows from position 0
+        cases = (("llama3-8b", 32, 8, 128, 0, args.attention_rows),)
+    for name, nh, nkv, hd, pos, rows in cases:
         max_seq = pos + rows
         keys = torch.randn((max_seq, nkv, hd), generator=g, device=dev)
         values = torch.randn((max_seq, nkv, hd), generator=g, device=dev)
@@ -1211,6 +1236,9 @@ def main():
                     help="decode-path linear layer: one JSON line per shape")
     ap.add_argument("--attention", action="store_true",
                     help="decode attention: one JSON line per case")
+    ap.add_argument("--attention-rows", type=int, default=0,
+                    help="prompt attention only: one Llama-3-8B chunk of this many "
+                         "rows, CUDA cores then tensor cores")
     ap.add_argument("--prefill", action="store_true",
                     help="whole-model prefill / decode through ForwardBatchCuda")
     ap.add_argument("--prefill-layers", type=int, default=4)
@@ -1243,6 +1271,9 @@ def main():
         return
     if args.linear:
         linear_bench(args)
+        return
+    if args.attention_rows:
+        attention_rows_bench(args)
         return
     if args.attention:
         attention_bench(args)
