@@ -21,6 +21,7 @@ flush is needed between steps.  Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import glob
 import json
 import subprocess
@@ -362,72 +363,77 @@ def e2e_run(step: LayerStep, steps: int, chunks: int = 8, numa: bool = True):
 GRAPH_REPEAT = 10
 
 
-def cold_timing(step: LayerStep, args, world):
-    """Steps whose working set is under 2 x L2 (back-to-back steps would
-    read it from L2): every step runs alone after an L2 eviction — a read of
-    a 512 MiB buffer, then a ~0.5 ms device sleep during which the host
-    enqueues the step's launches and events — so the events bracket only the
-    step's kernels; the median step and the median of each operator's events
-    inside it are kept.  Returns total ms over args.steps steps, per-op ms,
-    and the clock sampler."""
+def rotation_timing(steps, args, world):
+    """Steps whose working set is under 2 x L2: `steps` holds independent
+    copies of the step's inputs (3 x L2 in all), and one CUDA graph runs one
+    step on each copy in turn, so every step reads data that the steps
+    since its last turn have evicted from L2, while the launches pipeline as
+    they do in a model.  The graph is replayed back to back; per-operator
+    times come from graphs of that operator over every copy.  Returns total
+    ms over args.steps steps, per-op ms, and the clock sampler."""
     import torch
     import torch.distributed as dist
-    global _flush_buf
-    if _flush_buf is None:
-        _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
-    nops = len(step.ops)
-    totals, per_op = [], [[] for _ in range(nops)]
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()  # warm the capture stream once outside the graph
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=stream):
+                fn()
+        return g
+
+    def all_steps():
+        for st in steps:
+            st.step()
+
+    copies = len(steps)
+    step_graph = capture(all_steps)
+    op_graphs = [capture(lambda op=op: [st.launch(op) for st in steps]) for op in steps[0].ops]
+    replays = max(1, (args.steps + copies - 1) // copies)
+    for g in [step_graph] + op_graphs:
+        g.replay()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(torch.cuda.current_device())
     with sampler:
-        for _ in range(args.steps):
-            events = [torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
-            _flush_buf.sum()  # evicts L2, leaving only clean lines
-            torch.cuda._sleep(1_000_000)  # the host enqueues the step meanwhile
-            step.step(events)
-            torch.cuda.synchronize()
-            totals.append(events[0].elapsed_time(events[nops]))
-            for j in range(nops):
-                per_op[j].append(events[j].elapsed_time(events[j + 1]))
+        start.record()
+        for _ in range(replays):
+            step_graph.replay()
+        end.record()
+        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    return (statistics.median(totals) * args.steps,
-            [statistics.median(t) for t in per_op], sampler)
-
-
-def cold_op_ms(step: LayerStep, op: str, count: int) -> float:
-    """Median device time of one launch of `op` alone after an L2 eviction
-    (a 512 MiB read, then a ~0.5 ms device sleep during which the host
-    enqueues the launch)."""
-    import torch
-    global _flush_buf
-    if _flush_buf is None:
-        _flush_buf = torch.ones(512 * 1024 * 1024 // 4, device="cuda")
-    times = []
-    for _ in range(count):
-        _flush_buf.sum()
-        torch.cuda._sleep(1_000_000)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        step.launch(op)
-        e1.record()
+    total_ms = start.elapsed_time(end) * args.steps / (replays * copies)
+    op_ms = []
+    for g in op_graphs:
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(replays):
+            g.replay()
+        s1.record()
         torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    return statistics.median(times)
+        op_ms.append(s0.elapsed_time(s1) / (replays * copies))
+    del step_graph, op_graphs
+    return total_ms, op_ms, sampler
 
 
 def graph_timing(step: LayerStep, args, world):
     """Steps whose launches the host could not enqueue as fast as the GPU runs
     them: GRAPH_REPEAT steps are captured in one CUDA graph and replayed back
     to back (the step's working set is at least 2 x L2, so no step reads the
-    previous one's data from L2).  Per-operator times: an operator whose own
-    bytes reach 2 x L2 from a graph of GRAPH_REPEAT launches of it alone,
-    replayed back to back; a smaller one as the median of single launches
-    after an L2 eviction.  Returns total ms over args.steps steps, per-op ms,
-    and the clock sampler."""
+    previous one's data from L2).  Per-operator times come from a graph of
+    GRAPH_REPEAT launches of that operator alone, replayed back to back (an
+    operator whose own bytes are under 2 x L2 then reads them from L2: the
+    JSON line marks those).  Returns total ms over args.steps steps, per-op
+    ms, and the clock sampler."""
     import torch
     import torch.distributed as dist
     stream = torch.cuda.Stream()
@@ -444,9 +450,7 @@ def graph_timing(step: LayerStep, args, world):
         return g
 
     step_graph = capture(step.step)
-    op_bytes = step.bytes()
-    op_graphs = {op: capture(lambda op=op: step.launch(op)) for op in step.ops
-                 if op_bytes[op] >= 2 * L2_BYTES}
+    op_graphs = {op: capture(lambda op=op: step.launch(op)) for op in step.ops}
     replays = max(1, args.steps // GRAPH_REPEAT)
     for g in [step_graph] + list(op_graphs.values()):
         g.replay()
@@ -468,9 +472,6 @@ def graph_timing(step: LayerStep, args, world):
     total_ms = start.elapsed_time(end) * args.steps / (replays * GRAPH_REPEAT)
     op_ms = []
     for op in step.ops:
-        if op not in op_graphs:
-            op_ms.append(cold_op_ms(step, op, min(args.steps, 21)))
-            continue
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record()
@@ -648,8 +649,10 @@ def config_block(cfg, args, tokens_per_gpu, global_tokens):
 
 def l2_note(step_bytes: int) -> str:
     if step_bytes < 2 * L2_BYTES:
-        return (f"working set {step_bytes / 1e6:.1f} MB < 2 x L2 (126 MB): L2 evicted "
-                "(512 MiB read) before every step, median step")
+        copies = -(-3 * L2_BYTES // step_bytes)
+        return (f"inputs larger than L2: {copies} copies of the step's "
+                f"{step_bytes / 1e6:.1f} MB working set ({copies * step_bytes / 1e6:.0f} MB "
+                "in all), one step on each in turn; no flush")
     return "inputs larger than L2 (126 MB); no flush"
 
 
@@ -762,13 +765,20 @@ def gpu_arm(args, cfg):
     # spent a quarter of each step waiting on the host with direct launches)
     use_graph = args.graph == "on" or (args.graph == "auto" and (tokens <= 4096 or world > 1))
     # a working set under 2 x L2 would be read from L2 by back-to-back steps:
-    # such steps are timed one at a time after an L2 eviction
+    # such steps rotate over independent copies of their inputs (3 x L2 in
+    # all, each copy from its own seed)
     cold = sum(op_bytes.values()) < 2 * L2_BYTES
+    steps = [step]
+    if cold:
+        copies = -(-3 * L2_BYTES // sum(op_bytes.values()))
+        steps += [LayerStep(dataclasses.replace(cfg, seed=cfg.seed + 1000 * c), dev, tokens,
+                            pos_offset, ops) for c in range(1, copies)]
     for _ in range(args.warmup):
-        step.step()
+        for st in steps:
+            st.step()
     torch.cuda.synchronize()
     if cold:
-        total_ms, op_ms, sampler = cold_timing(step, args, world)
+        total_ms, op_ms, sampler = rotation_timing(steps, args, world)
     elif use_graph:
         total_ms, op_ms, sampler = graph_timing(step, args, world)
     else:
@@ -852,7 +862,7 @@ def gpu_arm(args, cfg):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3),
             "pinned_numa_node": getattr(step, "e2e_numa_node", None)},
-        "timing": ("direct launches, one step at a time after an L2 eviction" if cold
+        "timing": ("cuda graph replay over rotating input copies" if cold
                    else "cuda graph replay" if use_graph else "direct launches"),
         "launch_overlap": args.launch_overlap,
         "gpu_launches": args.steps * len(step.ops),
