@@ -19,9 +19,9 @@
 //   RmsNormClusterKernel — few rows (a decode batch, rows < 2 x SMs) with
 //                        cols > 1024: a thread-block cluster of S <= 8 CTAs
 //                        shares each row; every CTA reduces its column slice
-//                        and reads the other CTAs' partial sums of squares
-//                        through distributed shared memory, so S times more
-//                        SMs work on the batch.
+//                        and pushes its partial sum of squares into the
+//                        other CTAs' shared memory (one barrier), so S times
+//                        more SMs work on the batch.
 //   RmsNormScalarKernel— any other shape/alignment: two passes, the second
 //                        re-reading the row (from L2 for realistic sizes).
 // HBM roofline: 16*rows*cols + 4*cols bytes with a residual (read x, r;
@@ -162,17 +162,38 @@ __global__ void __launch_bounds__(1024) RmsNormBlockKernel(RmsArgs a) {
   }
 }
 
+// barrier.cluster in its two halves: Arrive marks this thread's arrival
+// (relaxed: nothing to publish yet, or release: its shared-memory writes to
+// other CTAs are published), Wait blocks until every thread of every CTA in
+// the cluster has arrived (acquire).
+__device__ __forceinline__ void ClusterArriveRelaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void ClusterArriveRelease() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void ClusterWait() {
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
 // One row per cluster (blockIdx.x = row), S = cluster size CTAs along y.
 // CTA rank r owns float4 columns [r*chunk, min((r+1)*chunk, c4)), NV per
-// thread.  The partial sums are combined in rank order (deterministic).
+// thread; its weight slice is loaded with the row.  Each CTA pushes its
+// partial sum of squares into slot r of every CTA's `partials`, so one
+// barrier delivers them all and no CTA reads another's memory afterwards
+// (it may then exit at once).  A first barrier phase, arrived at on entry
+// and waited on only before the pushes, guarantees that every CTA of the
+// cluster is running when its shared memory is written.  The partials are
+// summed in rank order (deterministic).
 template <int NV, bool RES>
 __global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk) {
   LaunchWait();  // the previous kernel on the stream has completed
   LaunchNext();
+  ClusterArriveRelaxed();  // this CTA has started
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float scratch[32];
-  __shared__ float partial;
+  __shared__ float partials[8];
   const int c4 = a.cols >> 2;
   const int rank = static_cast<int>(cluster.block_rank());
   const int ranks = static_cast<int>(cluster.num_blocks());
@@ -181,11 +202,13 @@ __global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk
   const int64_t row = blockIdx.x;
   const size_t off = static_cast<size_t>(row) * c4;
   const float4* x4 = reinterpret_cast<const float4*>(a.x) + off;
-  float4 v[NV];
+  const float4* w4 = reinterpret_cast<const float4*>(a.w);
+  float4 v[NV], wv[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int i = c_begin + threadIdx.x + blockDim.x * k;
     v[k] = i < c_end ? LoadStream(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[k] = i < c_end ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (RES) {
     const float4* r4 = reinterpret_cast<const float4*>(a.res) + off;
@@ -207,18 +230,19 @@ __global__ void __launch_bounds__(256) RmsNormClusterKernel(RmsArgs a, int chunk
 #pragma unroll
   for (int k = 0; k < NV; ++k) ss = SumSq(v[k], ss);
   ss = BlockSum(ss, scratch);
-  if (threadIdx.x == 0) partial = ss;
-  cluster.sync();  // every CTA's partial is visible cluster-wide
+  ClusterWait();  // every CTA of the cluster has started
+  if (static_cast<int>(threadIdx.x) < ranks)
+    *cluster.map_shared_rank(&partials[rank], static_cast<int>(threadIdx.x)) = ss;
+  ClusterArriveRelease();
+  ClusterWait();  // every CTA's partial is in this CTA's `partials`
   float total = 0.0f;
-  for (int r = 0; r < ranks; ++r) total += *cluster.map_shared_rank(&partial, r);
-  cluster.sync();  // no CTA leaves while others still read its partial
+  for (int r = 0; r < ranks; ++r) total += partials[r];
   const float inv = InvRms(total, a.n_f, a.eps);
-  const float4* w4 = reinterpret_cast<const float4*>(a.w);
   float4* y4 = reinterpret_cast<float4*>(a.y) + off;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int i = c_begin + threadIdx.x + blockDim.x * k;
-    if (i < c_end) StoreStream(y4 + i, Scale(v[k], inv, __ldg(w4 + i)));
+    if (i < c_end) StoreStream(y4 + i, Scale(v[k], inv, wv[k]));
   }
 }
 

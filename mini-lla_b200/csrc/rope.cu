@@ -18,7 +18,9 @@
 //   normal: a float4 holds pairs 2g, 2g+1 -> table float4 (c,s,c,s)
 //   NeoX:   float4s at g*4 and hd/2 + g*4 hold pairs 4g..4g+3 -> two table
 //           float4s
-// One CTA walks the (head, group) items of a token and grid-strides tokens.
+// One CTA walks the (head, group) items of a token and grid-strides tokens;
+// with too few tokens to fill every SM twice, RopeSplitKernel spreads each
+// token's items over several CTAs, one item per thread.
 // HBM roofline: 8 bytes per rotated float plus the position (and the bias
 // vectors once, L2-resident afterwards).
 #include <climits>
@@ -56,13 +58,9 @@ __device__ __forceinline__ void Rotate(float& x0, float& x1, float c, float s) {
 // every CTA streams one contiguous q row and one k row.  (Measured on B200
 // at 40 heads x 128: 6.27 TB/s, against 5.83 TB/s for one item per thread
 // over a flat grid and 5.73 TB/s for a 2-D token x chunk grid.)
-// With few tokens (a decode batch) a token's items are split over
-// gridDim.y CTAs so that every SM gets work: CTA (x, y) walks items
-// y*blockDim.x, stepping by gridDim.y*blockDim.x.
-// SPLIT is a template flag so that the unsplit form (large batches) keeps
-// full occupancy: its item loop is a chain of dependent load -> store steps,
-// and the extra index registers of the split form cost 2 of 8 CTAs per SM.
-template <bool NEOX, bool SPLIT>
+// (Launched for heads wider than 256 float4 groups; few tokens go to
+// RopeSplitKernel, narrower heads to RopeRowsKernel.)
+template <bool NEOX>
 __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
   LaunchWait();  // the previous kernel on the stream has completed
   LaunchNext();
@@ -73,13 +71,11 @@ __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
     const int64_t pos =
         a.positions != nullptr ? __ldg(a.positions + t) : a.position_base + t;
     const bool ok = pos >= 0 && pos < a.table_rows;
-    if (!ok && threadIdx.x == 0 && (!SPLIT || blockIdx.y == 0) &&
-        a.status != nullptr)
+    if (!ok && threadIdx.x == 0 && a.status != nullptr)
       atomicOr(a.status, MLB_STATUS_BAD_POSITION);
     const float4* trow = reinterpret_cast<const float4*>(
         a.table + static_cast<size_t>(ok ? pos : 0) * a.hd);
-    for (int it = SPLIT ? blockIdx.y * blockDim.x + threadIdx.x : threadIdx.x;
-         it < items; it += SPLIT ? gridDim.y * blockDim.x : blockDim.x) {
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
       const int head = it / groups;
       const int g = it - head * groups;
       const bool is_q = head < a.nq;
@@ -119,6 +115,69 @@ __global__ void __launch_bounds__(256) RopeVecKernel(RopeArgs a) {
         }
         StoreStream(lo, x0);
       }
+    }
+  }
+}
+
+// Few tokens (a decode batch): token t's (head, group) items are spread
+// over gridDim.y CTAs, one item per thread (the launch makes gridDim.y *
+// blockDim.x cover the items; a longer item range is walked in steps).  The
+// item's q / k (and bias) loads are issued before the position load, so a
+// thread waits for two DRAM round trips, position then (cos, sin), with its
+// data in flight alongside, and never for a load that follows a store.  The
+// bad-position status is set after the item is written, so that no branch
+// on the position stands between the loads and their uses.
+template <bool NEOX>
+__global__ void __launch_bounds__(256) RopeSplitKernel(RopeArgs a) {
+  LaunchWait();  // the previous kernel on the stream has completed
+  LaunchNext();
+  const int half = a.hd >> 1;
+  const int groups = NEOX ? (a.hd >> 3) : (a.hd >> 2);  // per head
+  const int items = (a.nq + a.nk) * groups;
+  const int first = blockIdx.y * blockDim.x + threadIdx.x;
+  const int step = gridDim.y * blockDim.x;
+  for (int64_t t = blockIdx.x; t < a.rows; t += gridDim.x) {
+    for (int it = first; it < items; it += step) {
+      const int head = it / groups;
+      const int g = it - head * groups;
+      const bool is_q = head < a.nq;
+      const int h = is_q ? head : head - a.nq;
+      float* base = is_q ? a.q + (static_cast<size_t>(t) * a.nq + h) * a.hd
+                         : a.k + (static_cast<size_t>(t) * a.nk + h) * a.hd;
+      float4* lo = reinterpret_cast<float4*>(base + 4 * g);
+      float4* hi = reinterpret_cast<float4*>(base + half + 4 * g);
+      float4 x0 = LoadStream(lo);
+      float4 x1 = NEOX ? LoadStream(hi) : x0;
+      const float* bias = is_q ? a.bq : a.bk;
+      if (bias != nullptr) {
+        const float* bh = bias + static_cast<size_t>(h) * a.hd;
+        x0 = AddRn(x0, __ldg(reinterpret_cast<const float4*>(bh + 4 * g)));
+        if (NEOX)
+          x1 = AddRn(x1, __ldg(reinterpret_cast<const float4*>(bh + half + 4 * g)));
+      }
+      const int64_t pos =
+          a.positions != nullptr ? __ldg(a.positions + t) : a.position_base + t;
+      const bool ok = pos >= 0 && pos < a.table_rows;
+      if (ok) {
+        const float4* trow =
+            reinterpret_cast<const float4*>(a.table + static_cast<size_t>(pos) * a.hd);
+        if (NEOX) {
+          const float4 cs0 = __ldg(trow + 2 * g);      // pairs 4g, 4g+1
+          const float4 cs1 = __ldg(trow + 2 * g + 1);  // pairs 4g+2, 4g+3
+          Rotate(x0.x, x1.x, cs0.x, cs0.y);
+          Rotate(x0.y, x1.y, cs0.z, cs0.w);
+          Rotate(x0.z, x1.z, cs1.x, cs1.y);
+          Rotate(x0.w, x1.w, cs1.z, cs1.w);
+        } else {
+          const float4 cs = __ldg(trow + g);  // pairs 2g, 2g+1
+          Rotate(x0.x, x0.y, cs.x, cs.y);
+          Rotate(x0.z, x0.w, cs.z, cs.w);
+        }
+      }
+      StoreStream(lo, x0);
+      if (NEOX) StoreStream(hi, x1);
+      if (!ok && it == 0 && a.status != nullptr)
+        atomicOr(a.status, MLB_STATUS_BAD_POSITION);
     }
   }
 }
@@ -276,14 +335,14 @@ extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
   if (vec) {
     // split tokens over several CTAs when they cannot fill every SM twice
     const int64_t fill = 2 * static_cast<int64_t>(SmCount());
-    int64_t split = rows < fill ? (fill + rows - 1) / rows : 1;
-    const int64_t max_split = (items + threads - 1) / threads;
-    if (split > max_split) split = max_split;
+    // (one item per thread: as many CTAs per token as its items need)
+    int64_t split = rows < fill ? (items + threads - 1) / threads : 1;
+    if (split > 65535) split = 65535;
     const dim3 grid2(grid.x, static_cast<unsigned>(split));
     const int G = neox ? hd / 8 : hd / 4;  // float4 groups per head
     if (split > 1) {
-      if (neox) Launch(RopeVecKernel<true, true>, grid2, threads, 0, s, a);
-      else Launch(RopeVecKernel<false, true>, grid2, threads, 0, s, a);
+      if (neox) Launch(RopeSplitKernel<true>, grid2, threads, 0, s, a);
+      else Launch(RopeSplitKernel<false>, grid2, threads, 0, s, a);
     } else if (G <= 256) {
       // heads per pass: as many as fit 128 threads (at least one), no more
       // than there are.  Measured on B200 in the layer-op step: 128-thread
@@ -296,8 +355,8 @@ extern "C" int mlb_rope_f32(float* q, float* k, const float* bq,
       if (neox) Launch(RopeRowsKernel<true, 1>, grid, rthreads, 0, s, a, G);
       else Launch(RopeRowsKernel<false, 1>, grid, rthreads, 0, s, a, G);
     } else {
-      if (neox) Launch(RopeVecKernel<true, false>, grid, threads, 0, s, a);
-      else Launch(RopeVecKernel<false, false>, grid, threads, 0, s, a);
+      if (neox) Launch(RopeVecKernel<true>, grid, threads, 0, s, a);
+      else Launch(RopeVecKernel<false>, grid, threads, 0, s, a);
     }
   } else {
     Launch(RopeScalarKernel, grid, 256, 0, s, a, neox);

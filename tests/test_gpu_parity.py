@@ -72,6 +72,22 @@ def test_rmsnorm_shapes_vs_oracle(cuda, oracle, rows, cols):
                what="plain")
 
 
+@pytest.mark.parametrize("rows,cols", [(2500, 896), (2400, 64), (300, 4096)])
+def test_rmsnorm_large_batches_vs_oracle(cuda, oracle, rows, cols):
+    """Batches that fill the SMs: eight rows per CTA for cols <= 1024 (the
+    weight loaded at the store), one CTA per row above."""
+    import torch
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols), dtype=np.float32)
+    r = rng.standard_normal((rows, cols), dtype=np.float32)
+    w = (rng.standard_normal(cols, dtype=np.float32) * 0.1 + 1).astype(np.float32)
+    want_y, want_h = oracle.rmsnorm(x, w, 1e-6, residual=r)
+    h = torch.full((rows, cols), float("nan"), device=cuda)
+    y = mlb.rms_norm(dev(x, cuda), dev(w, cuda), 1e-6, residual=dev(r, cuda), h_out=h)
+    assert_bitexact(host(h), want_h, "h")
+    assert_rel(host(y), want_y, what="y")
+
+
 def test_rmsnorm_in_place_and_unaligned(cuda, oracle):
     """h_out may alias x; without a residual y may alias x; views that are
     not 16-byte aligned take the scalar path and still match."""
@@ -123,7 +139,10 @@ def test_swiglu_kat_and_extremes(cuda):
                g["edge_o"], what="extremes")
 
 
-@pytest.mark.parametrize("n", [1, 3, 4, 1000, 4864 * 7, 1 << 20, (1 << 20) + 3])
+# 1 << 20 fits one wave of CTAs on a B200; 1.6 M to 4 M take two to four
+# waves, the last one partial
+@pytest.mark.parametrize("n", [1, 3, 4, 1000, 4864 * 7, 1 << 20, (1 << 20) + 3,
+                               1_600_000, 2_560_000, 2_880_000, 4_000_000])
 def test_swiglu_sizes_vs_oracle(cuda, oracle, n):
     rng = np.random.default_rng(n)
     g = rng.standard_normal(n, dtype=np.float32) * 3
@@ -148,6 +167,21 @@ def test_elementwise_bitexact_ops(cuda, oracle):
     assert_bitexact(host(mlb.add_bias(dev(odd, cuda), dev(ob, cuda))),
                     oracle.add(odd, np.broadcast_to(ob, odd.shape)), "bias scalar")
     # in place: out aliases an input
+    out = dev(a, cuda)
+    mlb.swiglu(out, bd, out=out)
+    assert_rel(host(out), oracle.swiglu(a, b), what="swiglu in place")
+
+
+@pytest.mark.parametrize("n", [1_600_000, 2_880_000])
+def test_elementwise_wave_sizes_in_place(cuda, oracle, n):
+    """Arrays of several waves of CTAs: the output aliasing an input, and
+    the bit-exact binary ops at the same sizes."""
+    rng = np.random.default_rng(n)
+    a = rng.standard_normal(n, dtype=np.float32)
+    b = rng.standard_normal(n, dtype=np.float32)
+    ad, bd = dev(a, cuda), dev(b, cuda)
+    assert_bitexact(host(mlb.add(ad, bd)), oracle.add(a, b), "add")
+    assert_bitexact(host(mlb.mul(ad, bd)), a * b, "mul")
     out = dev(a, cuda)
     mlb.swiglu(out, bd, out=out)
     assert_rel(host(out), oracle.swiglu(a, b), what="swiglu in place")
@@ -186,6 +220,27 @@ def test_softmax_shapes_vs_oracle(cuda, oracle, cols):
     assert_rel(host(mlb.softmax_rows(dev(x, cuda), dev(vl, cuda))), want)
     want_full, _ = oracle.softmax_rows(x)
     assert_rel(host(mlb.softmax_rows(dev(x, cuda))), want_full, what="full rows")
+
+
+@pytest.mark.parametrize("rows,cols", [(2100, 1024), (9000, 256), (3584, 256)])
+def test_softmax_large_masked_batch(cuda, oracle, rows, cols):
+    """Many warp-per-row rows (C1's 14 x 256 rows among them): causal
+    lengths plus a few bad ones, flagged and written as zeros."""
+    import torch
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols), dtype=np.float32) * 2
+    vl = (np.arange(rows) % cols + 1).astype(np.int32)
+    bad_rows = [5, rows // 2, rows - 1]
+    vl[bad_rows] = [0, cols + 1, -7]
+    want, bad = oracle.softmax_rows(x, vl)
+    assert bad != 0
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = host(mlb.softmax_rows(dev(x, cuda), dev(vl, cuda), status=status))
+    assert mlb.status_check(status) == mlb.STATUS_BAD_LENGTH
+    assert not got[bad_rows].any()
+    good = np.ones(rows, bool)
+    good[bad_rows] = False
+    assert_rel(got[good], want[good])
 
 
 def test_softmax_bad_lengths_flagged(cuda):
