@@ -51,12 +51,16 @@ struct AttnArgs {
   float scale;
 };
 
-// Number of position slices for a launch of `rows` query rows: enough CTAs
-// to cover every SM twice, at least kMinSlice positions per slice (of the
-// longest row).
+// Number of position slices for a launch of `rows` query rows: as many as
+// fill the kSliceCtasPerSm CTAs that every SM holds at once (the slice
+// kernel's shared-memory limit at head_dim 128), rounded down so that no CTA
+// waits for a second wave, and at least kMinSlice positions per slice (of
+// the longest row).  (Measured on B200, 32 / 8 heads x 128 at position
+// 16383: 55 slices at 3 CTAs per SM against 37 at 2.)
+constexpr int kSliceCtasPerSm = 3;
 int Splits(int n_kv_heads, int64_t visible, int64_t rows = 1) {
   const int64_t ctas = static_cast<int64_t>(n_kv_heads) * rows;
-  const int64_t want = (2 * static_cast<int64_t>(SmCount()) + ctas - 1) / ctas;
+  const int64_t want = kSliceCtasPerSm * static_cast<int64_t>(SmCount()) / ctas;
   const int64_t most = (visible + kMinSlice - 1) / kMinSlice;
   int64_t s = want < most ? want : most;
   if (s < 1) s = 1;
@@ -189,67 +193,88 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnPartialKernel(AttnArgs a)
   }
 }
 
-// out[h][i] = sum_s acc_s[i] * e^(m_s - M) / sum_s l_s * e^(m_s - M).
+// out[h][i] = sum_s acc_s[i] * f_s / sum_s l_s * f_s, f_s = e^(m_s - M),
+// M = max_s m_s (f_s = 0 for a slice that saw no position).  The CTA's
+// threads take the slices in parallel for M and for the factors (kept in
+// shared memory, `splits` floats) and sum l_s * f_s as a block tree; thread
+// i then adds its output's terms in slice order, loads independent of one
+// another.  (The slice loops of one thread each, one dependent L2 load per
+// slice, took ~13 us at 37 slices.)
 __global__ void __launch_bounds__(256) AttnCombineKernel(AttnArgs a) {
   LaunchWait();  // the previous kernel on the stream has completed
   LaunchNext();
+  extern __shared__ float factor[];  // [splits]
+  __shared__ float scratch[2][32];
   const int head = blockIdx.x;
   const int64_t row = blockIdx.y;
-  const float* base = a.scratch + (row * a.n_heads + head) * a.splits * (a.hd + 2);
+  const int stride = a.hd + 2;
+  const float* base = a.scratch + (row * a.n_heads + head) * a.splits * stride;
   float mm = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) mm = fmaxf(mm, base[s * (a.hd + 2)]);
+  for (int s = threadIdx.x; s < a.splits; s += blockDim.x)
+    mm = fmaxf(mm, base[static_cast<int64_t>(s) * stride]);
+  mm = BlockMax(mm, scratch[0]);
   float ll = 0.0f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float ms = base[s * (a.hd + 2)];
-    if (ms != -INFINITY) ll = fmaf(base[s * (a.hd + 2) + 1], expf(ms - mm), ll);
+  for (int s = threadIdx.x; s < a.splits; s += blockDim.x) {
+    const float ms = base[static_cast<int64_t>(s) * stride];
+    const float f = ms == -INFINITY ? 0.0f : expf(ms - mm);
+    factor[s] = f;
+    ll = fmaf(base[static_cast<int64_t>(s) * stride + 1], f, ll);
   }
+  ll = BlockSum(ll, scratch[1]);  // its barrier also publishes factor[]
   for (int i = threadIdx.x; i < a.hd; i += blockDim.x) {
+    const float* acc = base + 2 + i;
     float sum = 0.0f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = base[s * (a.hd + 2)];
-      if (ms != -INFINITY) sum = fmaf(base[s * (a.hd + 2) + 2 + i], expf(ms - mm), sum);
-    }
+#pragma unroll 8
+    for (int s = 0; s < a.splits; ++s)
+      sum = fmaf(acc[static_cast<int64_t>(s) * stride], factor[s], sum);
     a.out[(row * a.n_heads + head) * a.hd + i] = __fdiv_rn(sum, ll);
   }
 }
 
-// Position-parallel form of the slice kernel (head_dim 64 or 128): each
-// warp takes its slice's positions 16 at a time and stages those 16 K and V
-// rows in shared memory with cp.async (one wait per block, so every warp has
-// a whole block of loads in flight; ~17 KB per warp lets 3 CTAs share an
-// SM).  Lanes 2r and 2r + 1 score position block + r against all G query
-// heads, each over one half of the dimensions, and add their halves with one
-// shuffle — instead of a 5-shuffle reduction per dot product.  K rows are
-// padded and their second half stored with chunk index ^ 4, so the two
-// lanes of a position (and the 4 positions of a quarter-warp) read distinct
-// banks.  One warp max / sum per block and head feeds the online softmax;
-// P.V walks the block's positions with the probabilities broadcast by
-// shuffles and each lane accumulating DPL = hd / 32 dimensions of a V row
-// read from shared memory.  The 4 warps' states are merged and written as
-// the slice partial, as in AttnPartialKernel.
-constexpr int kLaneBlock = 16;
+// Position-parallel form of the slice kernel (head_dim 64 or 128).  Each
+// warp walks its slice's positions kQuadBlock = 8 at a time, double-buffered:
+// the K and V rows of its next block are copied into shared memory with
+// cp.async while the current block is computed (2 x ~8.7 KB per warp, so
+// 3 CTAs share an SM).  Lanes 4r .. 4r + 3 score position r of the block
+// against all G query heads, one quarter of the dimensions each, and add
+// the quarters with two shuffles.  Bank layout: chunk c (16 bytes) of
+// quarter j of a K row, and of each q vector, is stored at Q * j + (c ^ j)
+// (Q chunks per quarter) and K rows are padded by 16 floats, so the 8 lanes
+// of a quarter-warp (2 positions x 4 quarters) read 8 distinct bank groups
+// and the q reads are 4-address broadcasts.  Per block and head the online
+// softmax takes 3 shuffles for the max and 3 for the sum (the 4 lanes of a
+// position hold the same score); P.V walks the block's rows with the G
+// probabilities of a row broadcast from shared memory and each lane
+// accumulating DPL = hd / 32 dimensions of the V row.  The 4 warps' states
+// are merged and written as the slice partial, as in AttnPartialKernel.
+// (Measured on B200, 32 / 8 heads x 128 at position 16383: the form before,
+// 2 lanes per position over 16-position blocks loaded and then computed,
+// spent ~40 % of each block waiting for its own copies.)
+constexpr int kQuadBlock = 8;
 
 template <int HD4>
-__host__ __device__ constexpr int LaneKRowFloats() { return 4 * HD4 + 4; }
+__host__ __device__ constexpr int QuadKRowFloats() { return 4 * HD4 + 16; }
 template <int HD4>
-__host__ __device__ constexpr int LaneWarpFloats() {  // K block + V block
-  return kLaneBlock * (LaneKRowFloats<HD4>() + 4 * HD4);
+__host__ __device__ constexpr int QuadStageFloats() {  // one block: K rows + V rows
+  return kQuadBlock * (QuadKRowFloats<HD4>() + 4 * HD4);
 }
 
 template <int G, int HD4>
-__global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32) AttnQuadPartialKernel(AttnArgs a) {
   LaunchWait();  // the previous kernel on the stream has completed
   LaunchNext();
   constexpr int HD = 4 * HD4;
   constexpr int DPL = HD / 32;        // dimensions per lane in P.V (2 or 4)
-  constexpr int KRF = LaneKRowFloats<HD4>();
-  constexpr int HALF4 = HD4 / 2;      // float4 chunks per half row
-  // dynamic: q of the G heads, then per warp a staged block of K and V rows
-  // (the warps' final accumulators reuse that area once the loop is done)
+  constexpr int Q = HD4 / 4;          // 16-byte chunks per quarter (4 or 8)
+  constexpr int KRF = QuadKRowFloats<HD4>();
+  constexpr int SF = QuadStageFloats<HD4>();
+  static_assert(Q == 4 || Q == 8, "head_dim 64 or 128");
+  // dynamic: q of the G heads, then per warp two staged blocks of K and V
+  // rows (the warps' final accumulators reuse that area once the loop is done)
   extern __shared__ __align__(16) float lsm[];
-  float* qs = lsm;                   // [G][HD]
-  float* blk_all = lsm + G * HD;     // [kAttnWarps][K rows | V rows]
-  __shared__ __align__(16) float sm_p[kAttnWarps][kLaneBlock][G];  // a block's probabilities
+  float* qs = lsm;                   // [G][HD], quarter-swizzled
+  float* stages = lsm + G * HD;      // [kAttnWarps][2][K rows | V rows]
+  __shared__ __align__(16) float sm_p[kAttnWarps][kQuadBlock][G];  // a block's probabilities
   __shared__ float sm_m[kAttnWarps][G];
   __shared__ float sm_l[kAttnWarps][G];
   const int lane = threadIdx.x & 31;
@@ -265,13 +290,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
   const float* kbase = a.keys + static_cast<int64_t>(g) * HD;
   const float* vbase = a.values + static_cast<int64_t>(g) * HD;
 
-  for (int i = threadIdx.x; i < G * HD4; i += blockDim.x)
-    reinterpret_cast<float4*>(qs)[i] =
+  for (int i = threadIdx.x; i < G * HD4; i += blockDim.x) {
+    const int h = i / HD4, c = i - h * HD4;
+    const int j = c / Q, cq = c - j * Q;
+    reinterpret_cast<float4*>(qs)[h * HD4 + Q * j + (cq ^ j)] =
         __ldg(reinterpret_cast<const float4*>(q_row + static_cast<int64_t>(g) * G * HD) + i);
+  }
   __syncthreads();
 
-  const int pos = lane >> 1;  // position of this lane pair in the block
-  const int half = lane & 1;  // which half of the dimensions it scores
+  const int pos = lane >> 2;      // position of this lane quad in the block
+  const int quarter = lane & 3;   // which quarter of the dimensions it scores
   float m[G], l[G], acc[G][DPL];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -280,35 +308,54 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
 #pragma unroll
     for (int e = 0; e < DPL; ++e) acc[h][e] = 0.0f;
   }
-  float* kw = blk_all + warp * LaneWarpFloats<HD4>();
-  float* vw = kw + kLaneBlock * KRF;
-  for (int64_t blk = t_begin + static_cast<int64_t>(warp) * kLaneBlock; blk < t_end;
-       blk += kAttnWarps * kLaneBlock) {
-    const int n = static_cast<int>(t_end - blk < kLaneBlock ? t_end - blk : kLaneBlock);
-    // stage K and V rows blk .. blk + n - 1 (coalesced); K chunk c of the
-    // second half goes to c ^ 4
+  float* wst = stages + warp * 2 * SF;
+  // copies rows blk .. blk + n - 1 into stage `buf` (coalesced 16-byte
+  // chunks; K chunks quarter-swizzled into padded rows) as one cp.async group
+  const auto stage = [&](int buf, int64_t blk, int n) {
+    float* kw = wst + buf * SF;
+    float* vw = kw + kQuadBlock * KRF;
     for (int i = lane; i < n * HD4; i += 32) {
       const int r = i / HD4, c = i - r * HD4;
+      const int j = c / Q, cq = c - j * Q;
       const int64_t off = (blk + r) * kv_stride + 4 * c;
-      CopyAsync16(kw + r * KRF + 4 * (c >= HALF4 ? (c ^ 4) : c), kbase + off);
+      CopyAsync16(kw + r * KRF + 4 * (Q * j + (cq ^ j)), kbase + off);
       CopyAsync16(vw + r * HD + 4 * c, vbase + off);
     }
     CopyAsyncCommit();
-    CopyAsyncWait<0>();
+  };
+  // positions of the block that starts at b (b < t_end)
+  const auto block_len = [t_end](int64_t b) {
+    return static_cast<int>(t_end - b < kQuadBlock ? t_end - b : kQuadBlock);
+  };
+  constexpr int64_t kStep = static_cast<int64_t>(kAttnWarps) * kQuadBlock;
+  int64_t blk = t_begin + static_cast<int64_t>(warp) * kQuadBlock;
+  if (blk < t_end) stage(0, blk, block_len(blk));
+  for (int buf = 0; blk < t_end; blk += kStep, buf ^= 1) {
+    const int n = block_len(blk);
+    const int64_t next = blk + kStep;
+    if (next < t_end)
+      stage(buf ^ 1, next, block_len(next));
+    else
+      CopyAsyncCommit();  // an empty group keeps the count below uniform
+    CopyAsyncWait<1>();   // this block's copies have landed
     __syncwarp();
-    // half scores of position blk + pos
+    const float* kw = wst + buf * SF;
+    const float* vw = kw + kQuadBlock * KRF;
+    // this quarter's part of the scores of position blk + pos, its chunks
+    // in order (the physical slot of chunk c of quarter j is c ^ j)
     float sc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) sc[h] = 0.0f;
     if (pos < n) {
-      const float* kr = kw + pos * KRF;
-#pragma unroll 8
-      for (int c = 0; c < HALF4; ++c) {
-        const int cc = half * HALF4 + c;  // logical chunk
-        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * (half ? (cc ^ 4) : cc));
+      const float* kr = kw + pos * KRF + 4 * Q * quarter;
+      const float* qq = qs + 4 * Q * quarter;
+#pragma unroll
+      for (int c = 0; c < Q; ++c) {
+        const int pc = c ^ quarter;
+        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * pc);
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float4 qv = *reinterpret_cast<const float4*>(qs + h * HD + 4 * cc);
+          const float4 qv = *reinterpret_cast<const float4*>(qq + h * HD + 4 * pc);
           sc[h] = fmaf(qv.x, kv.x, sc[h]);
           sc[h] = fmaf(qv.y, kv.y, sc[h]);
           sc[h] = fmaf(qv.z, kv.z, sc[h]);
@@ -316,18 +363,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
         }
       }
     }
-    // online softmax of the block, the G heads' warp reductions interleaved
-    // (same butterfly order as WarpMax / WarpSum, so the same values; one
-    // head at a time left each shuffle's latency exposed)
+    // full dot products on all 4 lanes of a position, then the block's
+    // online softmax over its 8 positions (heads interleaved per shuffle)
     float p[G], score[G], bm[G], ps[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      const float dot = sc[h] + __shfl_xor_sync(0xffffffffu, sc[h], 1);
+      float dot = sc[h] + __shfl_xor_sync(0xffffffffu, sc[h], 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
       score[h] = pos < n ? __fmul_rn(dot, a.scale) : -INFINITY;
       bm[h] = score[h];
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int o = 16; o >= 4; o >>= 1)
 #pragma unroll
       for (int h = 0; h < G; ++h) bm[h] = fmaxf(bm[h], __shfl_xor_sync(0xffffffffu, bm[h], o));
     float alpha[G];
@@ -337,10 +384,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
       alpha[h] = expf(m[h] - m_new);  // 0 on the first block
       p[h] = pos < n ? expf(score[h] - m_new) : 0.0f;
       m[h] = m_new;
-      ps[h] = half ? 0.0f : p[h];  // each position's p sits on both lanes of its pair
+      ps[h] = p[h];
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int o = 16; o >= 4; o >>= 1)
 #pragma unroll
       for (int h = 0; h < G; ++h) ps[h] += __shfl_xor_sync(0xffffffffu, ps[h], o);
 #pragma unroll
@@ -350,7 +397,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
       for (int e = 0; e < DPL; ++e) acc[h][e] *= alpha[h];
     }
     // the block's probabilities, G per position, for every lane's P.V
-    if (half == 0 && pos < n) {
+    if (quarter == 0 && pos < n) {
 #pragma unroll
       for (int h = 0; h < G; ++h) sm_p[warp][pos][h] = p[h];
     }
@@ -386,11 +433,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
         for (int e = 0; e < DPL; ++e) acc[h][e] = fmaf(pr[h], v[e], acc[h][e]);
       }
     }
-    __syncwarp();  // every lane is done with this block before it is restaged
+    __syncwarp();  // every lane is done with this stage before it is refilled
   }
   // merge the 4 warps, then write the slice partial
-  __syncthreads();  // every warp is done with its rows: reuse the area
-  float* sm_acc = blk_all;  // [kAttnWarps][G][HD]
+  __syncthreads();  // every warp is done with its stages: reuse the area
+  float* sm_acc = stages;  // [kAttnWarps][G][HD]
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     if (lane == 0) {
@@ -426,11 +473,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnLanePartialKernel(AttnArg
 }
 
 template <int G, int HD4>
-int LaunchLane(const AttnArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr size_t kStage = static_cast<size_t>(kAttnWarps) * LaneWarpFloats<HD4>();
+int LaunchQuad(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+  constexpr size_t kStage = static_cast<size_t>(kAttnWarps) * 2 * QuadStageFloats<HD4>();
   constexpr size_t kAcc = static_cast<size_t>(kAttnWarps) * G * 4 * HD4;
-  constexpr size_t shm = sizeof(float) * (G * 4 * HD4 + (kStage > kAcc ? kStage : kAcc));
-  auto kernel = AttnLanePartialKernel<G, HD4>;
+  static_assert(kAcc <= kStage, "the merge reuses the stage area");
+  constexpr size_t shm = sizeof(float) * (G * 4 * HD4 + kStage);
+  auto kernel = AttnQuadPartialKernel<G, HD4>;
   if (shm > 48 * 1024 &&
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(shm)) != cudaSuccess) {
@@ -446,9 +494,9 @@ int LaunchPartial(const AttnArgs& a, int64_t rows, int nv, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(a.n_kv_heads), static_cast<unsigned>(a.splits),
                   static_cast<unsigned>(rows));
   if (a.hd == 128) {
-    return LaunchLane<G, 32>(a, grid, s);
+    return LaunchQuad<G, 32>(a, grid, s);
   } else if (a.hd == 64) {
-    return LaunchLane<G, 16>(a, grid, s);
+    return LaunchQuad<G, 16>(a, grid, s);
   } else if (nv == 1) {
     Launch(AttnPartialKernel<G, 1>, grid, kAttnWarps * 32, 0, s, a);
   } else {
@@ -831,7 +879,8 @@ int AttentionRows(const float* q, const float* keys, const float* values, float*
       case 8: rc = LaunchPartial<8>(a, rc_rows, nv, s); break;
     }
     if (rc != MLB_OK) return rc;
-    Launch(AttnCombineKernel, dim3(n_heads, static_cast<unsigned>(rc_rows)), hd < 256 ? ((hd + 31) / 32) * 32 : 256, 0, s, a);
+    Launch(AttnCombineKernel, dim3(n_heads, static_cast<unsigned>(rc_rows)),
+           hd < 256 ? ((hd + 31) / 32) * 32 : 256, sizeof(float) * a.splits, s, a);
     rc = CheckLaunch("attention");
     if (rc != MLB_OK) return rc;
   }
