@@ -38,7 +38,9 @@ def _magnitude(q, keys, values, position, n_heads, n_kv):
 @pytest.mark.parametrize("nh,nkv,hd,pos,max_seq", [
     (4, 2, 8, 0, 16), (8, 2, 64, 37, 64), (32, 8, 128, 300, 512),
     (14, 2, 64, 255, 256), (32, 32, 128, 2047, 2048), (28, 4, 128, 4095, 4096),
-    (8, 1, 256, 1000, 1024), (16, 2, 32, 9999, 10000), (64, 8, 128, 65, 70)])
+    (8, 1, 256, 1000, 1024), (16, 2, 32, 9999, 10000), (64, 8, 128, 65, 70),
+    # 157 slices whose partials exceed the combine's shared memory
+    (8, 1, 128, 20000, 20001)])
 def test_attention_decode_vs_oracle(cuda, oracle, nh, nkv, hd, pos, max_seq):
     import torch
     rng = np.random.default_rng(nh * 1000 + pos)
@@ -69,6 +71,13 @@ def test_attention_reuses_scratch_and_rejects_bad_input(cuda, oracle):
         want = oracle.attention_decode(q, keys.cpu().numpy(), values.cpu().numpy(),
                                        pos, nh, nkv)
         assert np.allclose(got.cpu().numpy(), want, rtol=0, atol=1e-5)
+    # scratch that starts 4 bytes past a 16-byte boundary: the slice
+    # combine reads the partials from global memory instead of staging them
+    odd = torch.empty(need + 1, device=cuda)[1:]
+    got = mlb.attention_decode(dev(q, cuda), keys, values, max_seq - 1, scratch=odd)
+    want = oracle.attention_decode(q, keys.cpu().numpy(), values.cpu().numpy(),
+                                   max_seq - 1, nh, nkv)
+    assert np.allclose(got.cpu().numpy(), want, rtol=0, atol=1e-5)
     with pytest.raises(IndexError):
         mlb.attention_decode(dev(q, cuda), keys, values, max_seq)
     with pytest.raises(ValueError):

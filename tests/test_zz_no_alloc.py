@@ -94,7 +94,7 @@ def test_noalloc_refuses_sizes_beyond_its_array():
         pytest.skip("no CUDA device")
     lib = mlb.load()
     dev = torch.device("cuda:0")
-    # 1000 kv heads x 8 query heads of 256 values: one slice each, 2.06 Mi
+    # 1000 kv heads x 8 query heads of 256 values: one slice each, 2.08 M
     # floats of partials
     n_heads, n_kv, hd, max_seq = 8000, 1000, 256, 100
     need = lib.mlb_attention_scratch_floats(n_heads, n_kv, hd, max_seq - 1)
