@@ -308,7 +308,9 @@ int64_t mlb_attention_scratch_floats(int n_heads, int n_kv_heads, int head_dim,
  * The visible positions are split over CTAs (flash-decoding); each CTA reads
  * a kv head's K/V rows once for all of its query heads and writes a partial
  * softmax state to `scratch` (caller-owned device memory of at least
- * mlb_attention_scratch_floats(...) floats), which a second kernel combines.
+ * mlb_attention_scratch_floats(...) floats), which a second kernel combines
+ * (through shared memory when the scratch is 16-byte aligned, as every
+ * cudaMalloc / torch allocation is; from global memory otherwise).
  * Within 1e-5 * sum_t w_t |v_t| of the reference.  MLB_ERR_RANGE when
  * position is outside [0, max_seq).
  */
