@@ -361,15 +361,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnQuadPartialKernel(AttnArg
   float* wst = stages + warp * 2 * SF;
   // copies rows blk .. blk + n - 1 into stage `buf` (coalesced 16-byte
   // chunks; K chunks quarter-swizzled into padded rows) as one cp.async group
+  // (a warp covers RPI rows per pass; lane l always copies chunk l % HD4 of
+  // rows l / HD4 + RPI * pass, so its offsets are fixed)
+  constexpr int RPI = 32 / HD4;
+  const int sc_c = lane % HD4;
+  const int sc_r0 = lane / HD4;
+  const int sc_kdst = 4 * (Q * (sc_c / Q) + ((sc_c % Q) ^ (sc_c / Q)));
   const auto stage = [&](int buf, int64_t blk, int n) {
-    float* kw = wst + buf * SF;
-    float* vw = kw + kQuadBlock * KRF;
-    for (int i = lane; i < n * HD4; i += 32) {
-      const int r = i / HD4, c = i - r * HD4;
-      const int j = c / Q, cq = c - j * Q;
-      const int64_t off = (blk + r) * kv_stride + 4 * c;
-      CopyAsync16(kw + r * KRF + 4 * (Q * j + (cq ^ j)), kbase + off);
-      CopyAsync16(vw + r * HD + 4 * c, vbase + off);
+    float* kw = wst + buf * SF + sc_kdst;
+    float* vw = wst + buf * SF + kQuadBlock * KRF + 4 * sc_c;
+    const float* ks = kbase + 4 * sc_c;
+    const float* vs = vbase + 4 * sc_c;
+#pragma unroll
+    for (int it = 0; it < kQuadBlock / RPI; ++it) {
+      const int r = sc_r0 + RPI * it;
+      if (r < n) {
+        const int64_t off = (blk + r) * kv_stride;
+        CopyAsync16(kw + r * KRF, ks + off);
+        CopyAsync16(vw + r * HD, vs + off);
+      }
     }
     CopyAsyncCommit();
   };
@@ -453,7 +463,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) AttnQuadPartialKernel(AttnArg
     }
     __syncwarp();
     // P.V over the block's positions (V row r: lane owns dims DPL * lane ..)
-    for (int r = 0; r < n; ++r) {
+#pragma unroll
+    for (int r = 0; r < kQuadBlock; ++r) {
+      if (r >= n) break;
       const float* vr = vw + r * HD + DPL * lane;
       float v[DPL];
       if (DPL == 4) {
