@@ -680,7 +680,6 @@ unsigned int TcWaitTimeouts();  // linear_tc.cu
 // gemv_tc.cu
 int GemvTcSplit(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
                 int tokens);
-int64_t GemvTcTiles(int count, const int64_t* n);
 int GemvTc(int qtype, int count, const void* const* w, const int64_t* n, int64_t k,
            const float* x, int tokens, float* const* y, int split, cudaStream_t s);
 unsigned int GemvTcWaitTimeouts();
@@ -691,15 +690,17 @@ unsigned int AttnTcWaitTimeouts();     // attention_tc.cu
 namespace {
 // mlb_set_gemv_path: 0 automatic, 1 CUDA cores only, 2 tensor cores where allowed
 int g_gemv_path = 0;
-// Automatic choice: the tensor-core GEMV once the launch's matrices fill
-// kGemvTcMinTiles 128-row tiles, or kGemvTcMinTilesBatch tiles from
-// kGemvTcBatch tokens on.  (B200, Q8_0: 4096 x 4096 at T = 1 16.4 us against
-// 14.4 us on the CUDA cores, at T = 4 18.4 against 20.5; 4096 x 14336 at
-// T = 4 28.7 against 63.5; 1024 x 4096 at T = 4 16.4 against 12.3; q / k / v
-// of LLaMA-3-8B together, 48 tiles, and every wider matrix gain at T = 1.)
-constexpr int64_t kGemvTcMinTiles = 40;
-constexpr int64_t kGemvTcMinTilesBatch = 16;
-constexpr int64_t kGemvTcBatch = 3;
+// Automatic choice, by the launch's weight blocks (rows x k / 32, all its
+// matrices): the tensor-core GEMV from kGemvTcMinBlocks1 blocks for one
+// matrix at one token, from kGemvTcMinBlocks otherwise (a group at one token
+// would take one CUDA-core launch per matrix).  Measured on B200, Q8_0, one
+// call per weight copy in a CUDA graph (tensor cores / CUDA cores): one
+// token: 14336 x 4096 18.2 / 22.2 us, 4096 x 14336 18.9 / 22.0, 11008 x 4096
+// 17.4 / 17.4, 6144 x 4096 12.3 / 11.5, 4096 x 4096 9.8 / 8.6; two tokens:
+// 4096 x 14336 19.3 / 32.3, 4096 x 4096 9.9 / 10.3, 2048 x 4096 11.7 / 6.9;
+// four tokens: 4096 x 4096 10.1 / 14.3, 2048 x 4096 12.2 / 8.9.
+constexpr int64_t kGemvTcMinBlocks1 = 1200 * 1024;
+constexpr int64_t kGemvTcMinBlocks = 400 * 1024;
 constexpr int kGemvTcTokens = 4;  // tokens per tensor-core pass
 }  // namespace
 
@@ -713,8 +714,10 @@ int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, in
   const int first = static_cast<int>(t_rows < kGemvTcTokens ? t_rows : kGemvTcTokens);
   if (GemvTcSplit(qtype, count, w, n, k, first) <= 0) return -1;
   if (g_gemv_path != 2) {
-    const int64_t tiles = GemvTcTiles(count, n);
-    if (tiles < kGemvTcMinTiles && (t_rows < kGemvTcBatch || tiles < kGemvTcMinTilesBatch))
+    int64_t rows = 0;
+    for (int m = 0; m < count; ++m) rows += n[m];
+    const int64_t blocks = rows * ((k + 31) / 32);
+    if (blocks < (count == 1 && t_rows == 1 ? kGemvTcMinBlocks1 : kGemvTcMinBlocks))
       return -1;
   }
   float* yy[3];

@@ -924,7 +924,6 @@ int GemvTcSplit(int qtype, int count, const void* const* w, const int64_t* n, in
   return GtSplit(qtype, tiles, k, GtTokenClass(tokens));
 }
 
-int64_t GemvTcTiles(int count, const int64_t* n) { return GtTiles(count, n); }
 
 // y[m][t] = W[m] . x[t] for t < tokens (1..4) and m < count on the tensor
 // cores, `split` ranks per tile (from GemvTcSplit).
