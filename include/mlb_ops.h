@@ -200,9 +200,11 @@ int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
  * within |y - y_ref| <= 1e-5 * sum_i |w_i x_i|.  Weights are read once per
  * group of 8 tokens; k % 32 != 0 or unaligned x take a scalar path that keeps
  * the reference's summation order.
- * Wide ggml matrices (Q8_0: k % 256 == 0, Q4_0 / Q4_1: k % 512 == 0,
- * k <= 4096, 16-byte aligned table) run on the int8 tensor cores instead,
- * up to 4 tokens per pass: the codes enter the MMA as stored and x as four
+ * Large ggml launches (Q8_0: k % 256 == 0, Q4_0 / Q4_1: k % 512 == 0,
+ * 16-byte aligned table; long rows split over a cluster of up to 8 CTAs)
+ * run on the int8 tensor cores instead once they hold enough weight blocks
+ * (rows x k / 32: 1.2 M for one matrix at one token, 400 K otherwise), up
+ * to 4 tokens per pass: the codes enter the MMA as stored and x as four
  * exact int8 digits per value relative to a power-of-two block scale
  * (|x_i - digits| <= 2^-27 max|x| of its block), within the same bound.
  */
