@@ -804,7 +804,8 @@ def gpu_arm(args, cfg):
     if args.no_e2e:
         e2e_ms, h2d, d2h = float("nan"), 0, 0
     else:
-        e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps, numa=bool(args.e2e_numa))
+        e2e_ms, h2d, d2h = e2e_run(step, args.e2e_steps, chunks=args.e2e_chunks,
+                                   numa=bool(args.e2e_numa))
     stats = torch.tensor([total_ms, e2e_ms] + op_ms, dtype=torch.float64,
                          device=dev)
     if world > 1:
@@ -860,7 +861,8 @@ def gpu_arm(args, cfg):
         "e2e": None if args.no_e2e else {
             "value": round(tokens_all / (e2e_ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": args.e2e_steps, "ms_per_step": round(e2e_ms, 3),
+            "steps": args.e2e_steps, "chunks": args.e2e_chunks,
+            "ms_per_step": round(e2e_ms, 3),
             "pinned_numa_node": getattr(step, "e2e_numa_node", None)},
         "timing": ("cuda graph replay over rotating input copies" if cold
                    else "cuda graph replay" if use_graph else "direct launches"),
@@ -1278,6 +1280,8 @@ def main():
                     help="every GPU runs its own T rows (default: the T rows "
                          "are split across the GPUs)")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="token chunks the e2e leg pipelines copies and compute over")
     ap.add_argument("--cpu-budget", type=float, default=20.0,
                     help="seconds of CPU work for the CPU legs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
