@@ -203,7 +203,8 @@ int mlb_embedding_row(const void* table, int qtype, int64_t vocab,
  * Large ggml launches (Q8_0: k % 256 == 0, Q4_0 / Q4_1: k % 512 == 0,
  * 16-byte aligned table; long rows split over a cluster of up to 8 CTAs)
  * run on the int8 tensor cores instead once they hold enough weight blocks
- * (rows x k / 32: 1.2 M for one matrix at one token, 400 K otherwise), up
+ * (rows x k / 32: for one matrix 1.2 M at one token in Q8_0, 2.4 M / 1.2 M
+ * at one / two tokens in Q4_0 / Q4_1; 400 K otherwise), up
  * to 4 tokens per pass: the codes enter the MMA as stored and x as four
  * exact int8 digits per value relative to a power-of-two block scale
  * (|x_i - digits| <= 2^-27 max|x| of its block), within the same bound.

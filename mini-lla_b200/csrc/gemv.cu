@@ -691,15 +691,22 @@ namespace {
 // mlb_set_gemv_path: 0 automatic, 1 CUDA cores only, 2 tensor cores where allowed
 int g_gemv_path = 0;
 // Automatic choice, by the launch's weight blocks (rows x k / 32, all its
-// matrices): the tensor-core GEMV from kGemvTcMinBlocks1 blocks for one
-// matrix at one token, from kGemvTcMinBlocks otherwise (a group at one token
-// would take one CUDA-core launch per matrix).  Measured on B200, Q8_0, one
+// matrices): the tensor-core GEMV from kGemvTcMinBlocks1 blocks for one Q8_0
+// matrix at one token (kGemvTcMinBlocks1Q4 / kGemvTcMinBlocks2Q4 for one
+// 4-bit matrix at one / two tokens), from kGemvTcMinBlocks otherwise (a
+// group at one token would take one CUDA-core launch per matrix).  Measured on B200, Q8_0, one
 // call per weight copy in a CUDA graph (tensor cores / CUDA cores): one
 // token: 14336 x 4096 18.2 / 22.2 us, 4096 x 14336 18.9 / 22.0, 11008 x 4096
 // 17.4 / 17.4, 6144 x 4096 12.3 / 11.5, 4096 x 4096 9.8 / 8.6; two tokens:
 // 4096 x 14336 19.3 / 32.3, 4096 x 4096 9.9 / 10.3, 2048 x 4096 11.7 / 6.9;
-// four tokens: 4096 x 4096 10.1 / 14.3, 2048 x 4096 12.2 / 8.9.
+// four tokens: 4096 x 4096 10.1 / 14.3, 2048 x 4096 12.2 / 8.9.  The 4-bit
+// formats halve the CUDA-core form's bytes but not the tensor-core form's
+// per-tile cost, so one matrix stays on the CUDA cores longer: Q4_0 at one
+// token 14336 x 4096 17.8 / 16.9 us, 11008 x 4096 17.5 / 13.6; at two
+// tokens 6144 x 4096 12.9 / 12.4, 14336 x 4096 19.3 / 23.9 (Q4_1 alike).
 constexpr int64_t kGemvTcMinBlocks1 = 1200 * 1024;
+constexpr int64_t kGemvTcMinBlocks1Q4 = 2400 * 1024;
+constexpr int64_t kGemvTcMinBlocks2Q4 = 1200 * 1024;
 constexpr int64_t kGemvTcMinBlocks = 400 * 1024;
 constexpr int kGemvTcTokens = 4;  // tokens per tensor-core pass
 }  // namespace
@@ -717,8 +724,11 @@ int GemvTcGroup(int count, const void* const* w, int qtype, const int64_t* n, in
     int64_t rows = 0;
     for (int m = 0; m < count; ++m) rows += n[m];
     const int64_t blocks = rows * ((k + 31) / 32);
-    if (blocks < (count == 1 && t_rows == 1 ? kGemvTcMinBlocks1 : kGemvTcMinBlocks))
-      return -1;
+    const bool q4 = qtype != MLB_Q8_0;
+    int64_t need = kGemvTcMinBlocks;
+    if (count == 1 && t_rows == 1) need = q4 ? kGemvTcMinBlocks1Q4 : kGemvTcMinBlocks1;
+    if (count == 1 && t_rows == 2 && q4) need = kGemvTcMinBlocks2Q4;
+    if (blocks < need) return -1;
   }
   float* yy[3];
   for (int64_t t0 = 0; t0 < t_rows; t0 += kGemvTcTokens) {
