@@ -773,6 +773,15 @@ def gpu_arm(args, cfg):
         copies = -(-3 * L2_BYTES // sum(op_bytes.values()))
         steps += [LayerStep(dataclasses.replace(cfg, seed=cfg.seed + 1000 * c), dev, tokens,
                             pos_offset, ops) for c in range(1, copies)]
+    direct = not cold and not use_graph
+    if direct:
+        # NVML set-up (slow) and the events before the warm-up, so that the
+        # warm-up steps lead straight into the timed ones with no idle gap
+        events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
+                  for _ in range(args.steps)]
+        sampler = ClockSampler(local)
+        if world > 1:
+            dist.barrier()
     for _ in range(args.warmup):
         for st in steps:
             st.step()
@@ -782,12 +791,9 @@ def gpu_arm(args, cfg):
     elif use_graph:
         total_ms, op_ms, sampler = graph_timing(step, args, world)
     else:
-        events = [[torch.cuda.Event(enable_timing=True) for _ in range(nops + 1)]
-                  for _ in range(args.steps)]
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        sampler = ClockSampler(local)
         with sampler:
             for i in range(args.steps):
                 step.step(events[i])
