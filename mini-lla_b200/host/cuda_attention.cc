@@ -108,6 +108,18 @@ CudaTensor CudaAttention(const CudaTensor& q, const CudaKvCache& cache,
   return output;
 }
 
+CudaKvRows CudaKvCacheRows(CudaKvCache* cache, int layer, int position, int rows) {
+  if (cache == nullptr) throw std::invalid_argument("CudaKvCacheRows: null cache");
+  if (rows < 1) throw std::invalid_argument("CudaKvCacheRows: rows < 1");
+  CheckCache(*cache, layer, position);
+  CheckCache(*cache, layer, position + rows - 1);
+  const size_t offset = static_cast<size_t>(position) * cache->kv_heads() * cache->head_dim();
+  // the cache's layer buffers are device memory it owns; Keys()/Values() hand
+  // them out read-only, the writes go through the same addresses
+  return {const_cast<float*>(cache->Keys(layer)) + offset,
+          const_cast<float*>(cache->Values(layer)) + offset};
+}
+
 void CudaKvCacheWriteRows(CudaKvCache* cache, int layer, int position,
                           const CudaTensor& keys, const CudaTensor& values) {
   if (cache == nullptr) throw std::invalid_argument("CudaKvCacheWriteRows: null cache");

@@ -7,8 +7,9 @@
 // token.  Here a pass takes up to max_rows tokens of consecutive positions
 // through the same steps as [rows, .] tensors: the linears read each weight
 // on the tensor cores from 48 rows on (mlb_linear_rows_f32; q / k / v and
-// gate / up as one grouped launch each), RMSNorm / SwiGLU / bias + RoPE /
-// the K/V write / causal attention run once per layer over all rows, and
+// gate / up as one grouped launch each, that q / k / v launch writing K and
+// V straight into their KV-cache rows), RMSNorm / SwiGLU / bias + RoPE /
+// causal attention run once per layer over all rows, and
 // each residual add is fused into the RMSNorm that follows it.  Only the
 // last row of the batch goes through the final norm and the output
 // projection, since ForwardBatch returns the last token's logits.
@@ -161,21 +162,26 @@ Tensor ForwardBatchCuda(Context& context, const Model& model, const MiniBatch& b
         norm = CudaAddRmsNormRows(ffn, &x, *l.attention_norm, eps, &h);
         x = std::move(h);
       }
-      CudaTensor q, k, v;
-      if (SameShape(*l.wq, *l.wk) && SameShape(*l.wq, *l.wv)) {  // one launch
-        std::vector<CudaTensor> qkv = CudaLinearRowsGroup(norm, {l.wq, l.wk, l.wv});
-        q = std::move(qkv[0]);
-        k = std::move(qkv[1]);
-        v = std::move(qkv[2]);
+      CudaTensor q;
+      if (SameShape(*l.wq, *l.wk) && SameShape(*l.wq, *l.wv)) {
+        // one launch, K and V written straight into their cache rows (the
+        // cache holds consecutive positions contiguously), where the bias
+        // and RoPE are then applied: no separate K / V write
+        const CudaKvRows kv = CudaKvCacheRows(&context.cuda_cache, layer, position, rows);
+        q = CudaTensor(std::vector<int>{rows, l.wq->rows});
+        CudaLinearRowsGroupInto(norm, {l.wq, l.wk, l.wv}, {q.data(), kv.keys, kv.values});
+        if (l.bv != nullptr) CudaAddBiasRowsInPlace(kv.values, rows, *l.bv);
+        CudaRopeRowsInPlace(q.data(), kv.keys, l.bq, l.bk, positions, config.rope_theta,
+                            config.n_heads, config.n_kv_heads, head_dim, config.rope_type);
       } else {
         q = CudaLinearRows(norm, *l.wq);
-        k = CudaLinearRows(norm, *l.wk);
-        v = CudaLinearRows(norm, *l.wv);
+        CudaTensor k = CudaLinearRows(norm, *l.wk);
+        CudaTensor v = CudaLinearRows(norm, *l.wv);
+        if (l.bv != nullptr) v = CudaAddBiasRows(v, l.bv);
+        CudaRopeRows(&q, &k, l.bq, l.bk, positions, config.rope_theta, config.n_heads,
+                     config.n_kv_heads, head_dim, config.rope_type);
+        CudaKvCacheWriteRows(&context.cuda_cache, layer, position, k, v);
       }
-      if (l.bv != nullptr) v = CudaAddBiasRows(v, l.bv);
-      CudaRopeRows(&q, &k, l.bq, l.bk, positions, config.rope_theta, config.n_heads,
-                   config.n_kv_heads, head_dim, config.rope_type);
-      CudaKvCacheWriteRows(&context.cuda_cache, layer, position, k, v);
       const CudaTensor attention =
           CudaAttentionRows(q, context.cuda_cache, layer, position, config.n_heads,
                             config.n_kv_heads, head_dim);

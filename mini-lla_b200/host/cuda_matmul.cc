@@ -75,9 +75,13 @@ CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight) {
   return output;
 }
 
-std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
-                                            const std::vector<const CudaWeight*>& weights) {
-  if (weights.empty() || weights.size() > 3) {
+namespace {
+
+// The checks and the launch of CudaLinearRowsGroup, writing weight m's
+// output to y[m] (rows x weights[m]->rows floats).
+void LinearRowsGroupTo(const CudaTensor& x, const std::vector<const CudaWeight*>& weights,
+                       const std::vector<float*>& y) {
+  if (weights.empty() || weights.size() > 3 || y.size() != weights.size()) {
     throw std::invalid_argument("CudaLinearRowsGroup: 1 to 3 weights");
   }
   const CudaWeight& first = *weights.front();
@@ -90,29 +94,55 @@ std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
     throw std::invalid_argument("CudaLinearRowsGroup: input size mismatch");
   }
   const int rows = static_cast<int>(x.Size() / static_cast<size_t>(first.cols));
-  std::vector<CudaTensor> outputs;
+  if (rows == 0) return;
   const void* w[3];
   int64_t n[3];
-  float* y[3];
+  float* yy[3];
   for (size_t m = 0; m < weights.size(); ++m) {
-    outputs.emplace_back(std::vector<int>{rows, weights[m]->rows});
+    if (y[m] == nullptr) throw std::invalid_argument("CudaLinearRowsGroup: null output");
     w[m] = weights[m]->buffer.data();
     n[m] = weights[m]->rows;
-    y[m] = outputs.back().data();
+    yy[m] = y[m];
   }
-  if (rows == 0) return outputs;
   const int64_t need = mlb_linear_rows_scratch_floats(first.cols, rows);
   DeviceBuffer scratch;
   scratch.Reset(static_cast<size_t>(need) * sizeof(float));
   const int rc = mlb_linear_rows_group_f32(
-      static_cast<int>(weights.size()), w, QType(first.type), n, first.cols, x.data(), rows, y,
+      static_cast<int>(weights.size()), w, QType(first.type), n, first.cols, x.data(), rows, yy,
       static_cast<float*>(scratch.data()), need, nullptr);
   if (rc != MLB_OK) {
     const std::string message = std::string("CudaLinearRowsGroup: ") + mlb_last_error();
     if (rc == MLB_ERR_ARG) throw std::invalid_argument(message);
     throw std::runtime_error(message);
   }
+}
+
+}  // namespace
+
+std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
+                                            const std::vector<const CudaWeight*>& weights) {
+  if (weights.empty() || weights.size() > 3) {
+    throw std::invalid_argument("CudaLinearRowsGroup: 1 to 3 weights");
+  }
+  for (const CudaWeight* w : weights) {
+    if (w == nullptr || w->cols <= 0) {
+      throw std::invalid_argument("CudaLinearRowsGroup: weights differ in format or width");
+    }
+  }
+  const int rows = static_cast<int>(x.Size() / static_cast<size_t>(weights.front()->cols));
+  std::vector<CudaTensor> outputs;
+  std::vector<float*> y;
+  for (const CudaWeight* w : weights) {
+    outputs.emplace_back(std::vector<int>{rows, w->rows});
+    y.push_back(outputs.back().data());
+  }
+  LinearRowsGroupTo(x, weights, y);
   return outputs;
+}
+
+void CudaLinearRowsGroupInto(const CudaTensor& x, const std::vector<const CudaWeight*>& weights,
+                             const std::vector<float*>& outputs) {
+  LinearRowsGroupTo(x, weights, outputs);
 }
 
 }  // namespace mini_lla

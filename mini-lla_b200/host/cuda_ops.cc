@@ -359,6 +359,14 @@ CudaTensor CudaAddBiasRows(const CudaTensor& value, const CudaWeight* bias) {
   return output;
 }
 
+void CudaAddBiasRowsInPlace(float* value, int64_t rows, const CudaWeight& bias) {
+  const int64_t cols = static_cast<int64_t>(WeightSize(bias));
+  if (rows < 0 || cols <= 0) throw std::invalid_argument("CudaAddBiasRows: bad size");
+  if (rows == 0) return;
+  if (value == nullptr) throw std::invalid_argument("CudaAddBiasRows: null value");
+  Check(mlb_add_bias_f32(value, F32(bias), value, rows, cols, nullptr), "CudaAddBiasRows");
+}
+
 CudaTensor CudaSwiGlu(const CudaTensor& gate, const CudaTensor& up) {
   if (gate.shape() != up.shape()) {
     throw std::invalid_argument("CudaSwiGlu: shape mismatch");
@@ -384,6 +392,18 @@ void CudaRopeRows(CudaTensor* q, CudaTensor* k, const CudaWeight* bq,
       k->Size() != rows * n_kv_heads * head_dim) {
     throw std::invalid_argument("CudaRopeRows: q/k size mismatch");
   }
+  CudaRopeRowsInPlace(q->data(), k->data(), bq, bk, positions, theta, n_heads, n_kv_heads,
+                      head_dim, rope_type);
+}
+
+void CudaRopeRowsInPlace(float* q, float* k, const CudaWeight* bq, const CudaWeight* bk,
+                         const std::vector<int>& positions, float theta, int n_heads,
+                         int n_kv_heads, int head_dim, RopeType rope_type) {
+  RequireRope(theta, head_dim, "CudaRopeRows");
+  const size_t rows = positions.size();
+  if (rows > 0 && (q == nullptr || (n_kv_heads > 0 && k == nullptr))) {
+    throw std::invalid_argument("CudaRopeRows: null q or k");
+  }
   if ((bq != nullptr && WeightSize(*bq) != static_cast<size_t>(n_heads) * head_dim) ||
       (bk != nullptr && WeightSize(*bk) != static_cast<size_t>(n_kv_heads) * head_dim)) {
     throw std::invalid_argument("CudaRopeRows: bias size mismatch");
@@ -403,7 +423,7 @@ void CudaRopeRows(CudaTensor* q, CudaTensor* k, const CudaWeight* bq,
       theta, head_dim, int64_t{max_position} + 1, &table_rows);
   const int neox = rope_type == RopeType::kNeoX ? 1 : 0;
   if (consecutive) {
-    Check(mlb_rope_f32(q->data(), k->data(), bq ? F32(*bq) : nullptr,
+    Check(mlb_rope_f32(q, k, bq ? F32(*bq) : nullptr,
                        bk ? F32(*bk) : nullptr, nullptr, positions[0], table,
                        table_rows, static_cast<int64_t>(rows), n_heads,
                        n_kv_heads, head_dim, neox, nullptr, nullptr),
@@ -411,7 +431,7 @@ void CudaRopeRows(CudaTensor* q, CudaTensor* k, const CudaWeight* bq,
     return;
   }
   const DeviceBuffer device_positions = UploadInts(positions);
-  Check(mlb_rope_f32(q->data(), k->data(), bq ? F32(*bq) : nullptr,
+  Check(mlb_rope_f32(q, k, bq ? F32(*bq) : nullptr,
                      bk ? F32(*bk) : nullptr,
                      static_cast<const int32_t*>(device_positions.data()), 0,
                      table, table_rows, static_cast<int64_t>(rows), n_heads,

@@ -12,6 +12,7 @@
 #define MINI_LLA_INCLUDE_MINI_LLAMA_CUDA_LAYER_OPS_H_
 
 #include <cstddef>
+#include <cstdint>
 #include <functional>
 #include <utility>
 #include <vector>
@@ -44,6 +45,13 @@ void CudaRopeRows(CudaTensor* q, CudaTensor* k, const CudaWeight* bq,
                   float theta, int n_heads, int n_kv_heads, int head_dim,
                   RopeType rope_type);
 
+// CudaRopeRows on device memory the caller owns: q holds positions.size() x
+// n_heads x head_dim floats, k positions.size() x n_kv_heads x head_dim (for
+// instance the K rows of a KV cache, rotated where they are stored).
+void CudaRopeRowsInPlace(float* q, float* k, const CudaWeight* bq, const CudaWeight* bk,
+                         const std::vector<int>& positions, float theta, int n_heads,
+                         int n_kv_heads, int head_dim, RopeType rope_type);
+
 // Softmax of the first valid_len[r] entries of each row of x [rows, cols],
 // zeros after; valid_len null means full rows.
 CudaTensor CudaSoftmaxRows(const CudaTensor& x,
@@ -64,9 +72,28 @@ CudaTensor CudaLinearRows(const CudaTensor& x, const CudaWeight& weight);
 std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
                                             const std::vector<const CudaWeight*>& weights);
 
+// CudaLinearRowsGroup writing weight m's output to outputs[m], device memory
+// of rows x weights[m]->rows floats that the caller owns (for instance K and
+// V straight into their KV-cache rows).
+void CudaLinearRowsGroupInto(const CudaTensor& x, const std::vector<const CudaWeight*>& weights,
+                             const std::vector<float*>& outputs);
+
 // value[r] + bias for every row of value [rows, bias size] (AddBias,
 // forward.cc:36-47, for a batch of tokens); a null bias copies value.
 CudaTensor CudaAddBiasRows(const CudaTensor& value, const CudaWeight* bias);
+
+// The same add in place on rows x bias-size floats of device memory.
+void CudaAddBiasRowsInPlace(float* value, int64_t rows, const CudaWeight& bias);
+
+// Device addresses of rows [position, position + rows) of `layer` in the
+// cache's K and V buffers (rows x kv_heads x head_dim floats each, owned by
+// the cache), for kernels that write K / V where they are stored.
+// std::out_of_range when the rows or the layer leave the cache.
+struct CudaKvRows {
+  float* keys;
+  float* values;
+};
+CudaKvRows CudaKvCacheRows(CudaKvCache* cache, int layer, int position, int rows);
 
 // Writes the K/V of rows consecutive tokens (keys, values [rows, kv_heads *
 // head_dim]) to positions [position, position + rows) of `layer`
