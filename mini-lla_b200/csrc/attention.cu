@@ -34,7 +34,7 @@ namespace {
 constexpr int kAttnWarps = 4;
 constexpr int kMaxGroup = 8;      // query heads per kv head handled per CTA
 constexpr int kMaxHdVec = 2;      // float4 per lane: hd <= 256
-constexpr int kMinSlice = 128;    // positions per slice at least (4 warps x 32)
+constexpr int kMinSlice = 128;    // positions per slice at least (but see Splits)
 // A slice partial is (m, l, two unused floats, acc[hd]): acc rows start
 // 16 bytes after the record, so they stay 16-byte aligned for the combine's
 // cp.async copies.
@@ -55,18 +55,32 @@ struct AttnArgs {
   float scale;
 };
 
-// Number of position slices for a launch of `rows` query rows: as many as
-// fill the kSliceCtasPerSm CTAs that every SM holds at once (the slice
-// kernel's shared-memory limit at head_dim 128), rounded down so that no CTA
-// waits for a second wave, and at least kMinSlice positions per slice (of
-// the longest row).  (Measured on B200, 32 / 8 heads x 128 at position
-// 16383: 55 slices at 3 CTAs per SM against 37 at 2.)
+// Number of position slices for a launch of `rows` query rows (of the
+// longest row's positions), the largest of: slices of kMinSlice positions up
+// to the kSliceCtasPerSm CTAs that every SM holds at once (the slice
+// kernel's shared-memory limit at head_dim 128; rounded down so that no CTA
+// waits for a second wave); slices of 64 positions up to 2 CTAs per SM; of
+// 32 positions up to one CTA per SM.  Short caches get more, shorter
+// slices while the grid is small; long ones keep slices of 128 positions or
+// more.  Measured on B200 (a CUDA graph of calls over cache copies), 32 / 8
+// heads x 128, slices of 128 / 64 / 32 positions: position 511 8.8 / 6.7 /
+// 5.9 us, 2047 9.8 / 9.4 / 11.2 (440 CTAs of 37 positions: fixed costs
+// dominate), 4095 with 74-position slices at 3 CTAs per SM 14.5 against
+// 12.8; 16383 30.7 (55 slices, 3 CTAs per SM; 37 slices at 2 per SM were
+// slower).
 constexpr int kSliceCtasPerSm = 3;
 int Splits(int n_kv_heads, int64_t visible, int64_t rows = 1) {
   const int64_t ctas = static_cast<int64_t>(n_kv_heads) * rows;
-  const int64_t want = kSliceCtasPerSm * static_cast<int64_t>(SmCount()) / ctas;
-  const int64_t most = (visible + kMinSlice - 1) / kMinSlice;
-  int64_t s = want < most ? want : most;
+  const int64_t sms = SmCount();
+  const auto slices = [&](int64_t positions, int64_t per_sm) {
+    const int64_t by_length = (visible + positions - 1) / positions;
+    const int64_t by_grid = per_sm * sms / ctas;
+    return by_length < by_grid ? by_length : by_grid;
+  };
+  int64_t s = slices(kMinSlice, kSliceCtasPerSm);
+  const int64_t mid = slices(64, 2), small = slices(32, 1);
+  if (mid > s) s = mid;
+  if (small > s) s = small;
   if (s < 1) s = 1;
   return static_cast<int>(s);
 }
