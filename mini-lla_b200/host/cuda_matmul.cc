@@ -132,6 +132,7 @@ std::vector<CudaTensor> CudaLinearRowsGroup(const CudaTensor& x,
   const int rows = static_cast<int>(x.Size() / static_cast<size_t>(weights.front()->cols));
   std::vector<CudaTensor> outputs;
   std::vector<float*> y;
+  outputs.reserve(weights.size());
   for (const CudaWeight* w : weights) {
     outputs.emplace_back(std::vector<int>{rows, w->rows});
     y.push_back(outputs.back().data());
