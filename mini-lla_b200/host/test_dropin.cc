@@ -413,6 +413,13 @@ void TestAttention(std::mt19937& rng) {
     Expect(Throws([&] { cache.Write(layer, c.max_seq, CudaTensor({c.n_kv * c.hd}),
                                     CudaTensor({c.n_kv * c.hd})); }),
            "CudaKvCache::Write out of range throws");
+    const size_t at = static_cast<size_t>(c.position) * c.n_kv * c.hd;
+    const CudaKvRows kv = CudaKvCacheRows(&cache, layer, c.position, 1);
+    Expect(kv.keys == cache.Keys(layer) + at && kv.values == cache.Values(layer) + at,
+           "CudaKvCacheRows addresses the cache's own rows");
+    Expect(Throws([&] { CudaKvCacheRows(&cache, layer, c.max_seq - 1, 2); }) &&
+               Throws([&] { CudaKvCacheRows(&cache, c.layers, 0, 1); }),
+           "CudaKvCacheRows past the cache throws");
   }
 }
 
